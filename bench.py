@@ -1,0 +1,362 @@
+"""Benchmark of the paged verify-attention hot path (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload target_verify_8b|draft_decode_0p6b|long_verify_8b_k4|long_verify_8b_k8]
+                    [--kernel auto|decode|verify]
+
+Metric: paged verify-attention achieved HBM TB/s at the
+Qwen3-8B shape.  A *step* is the attention of one Target verify forward: one
+``paged_attention`` call per layer (36 calls), each over the layer's own slice
+of a 24,576-block paged KV pool (58 GB of fp16 K+V), for 16 requests verified
+at depth 4 with prefix lengths U[256, 4096].  Every step therefore streams
+5.1 GB of distinct KV (inputs larger than the 126 MB L2, no flush needed).
+
+``value``  = algorithmic bytes (unique K+V + q + o + block-table entries) of
+             all ranks / max-over-ranks device time, with inputs in HBM.
+``e2e``    = the same bytes / device time of the user-facing call
+             (``nebulasd_b200.kernels.paged_attention`` with an ``infer_state``),
+             with every step's q rows, lengths, seq ids and block table copied
+             from pinned host memory and every step's o copied back inside the
+             timed region.
+Multi-GPU runs (torchrun) are weak scaling: each rank owns its own 16
+requests and pool, no collective on the path.  ``--impl reference`` times the
+reference semantics (the fp32 PyTorch-eager oracle) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+import types
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged verify-attn achieved HBM TB/s (% peak), Qwen3-8B shape, 1/2/4/8 B200"
+UNIT = "TB/s"
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--workload", default="target_verify_8b")
+    ap.add_argument("--kernel", default="auto", choices=("auto", "decode", "verify"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    return ap.parse_args()
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic(workload: str, kernel: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    f = ROOT / "profiles" / f"{kernel}_attn_{workload}.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (median SM MHz, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.out = out
+        return False
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        busy = [s for s in sm if mx and s > 0.3 * mx] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_workload(name: str, seed: int, device):
+    from nebulasd_b200.workloads import CONFIGS, make_paged_batch
+    cfg = dict(CONFIGS[name])
+    layers = cfg.pop("num_layers", 1)
+    b = make_paged_batch(seed, num_layers=layers, cur_layer=0, device=device, **cfg)
+    return b, layers, cfg
+
+
+def step_bytes(b, layers: int) -> int:
+    """Algorithmic bytes of one step: per layer unique K+V, q and o rows, block-table entries."""
+    kv = b.kv_bytes()
+    qo = 2 * b.q.numel() * b.q.element_size()
+    tables = 4 * sum(math.ceil((c + d + 1) / 16) for c, d in zip(b.ctx, b.depths))
+    return layers * (kv + qo + tables)
+
+
+def run_ours(args):
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from nebulasd_b200 import _lib
+    from nebulasd_b200.kernels import paged_attention, paged_attention_raw
+    from nebulasd_b200.kernels.paged_attn import choose_kernel, set_kernel
+    set_kernel(args.kernel)
+
+    b, layers, cfg = build_workload(args.workload, 1234 + 7919 * rank, dev)
+    kernel = choose_kernel(b.num_q_heads, b.num_kv_heads)
+    kname = "verify" if kernel == _lib.NEB_ATTN_VERIFY else "decode"
+    o = torch.empty_like(b.q)
+    stream = torch.cuda.current_stream(dev)
+    scale = b.q.shape[-1] ** -0.5
+
+    def step():
+        for layer in range(layers):
+            paged_attention_raw(b.q, b.k_cache, b.v_cache, b.block_table, b.seq_lens, b.seq_ids, layer, scale, o,
+                                kernel=kernel, stream=stream)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t_soak = time.time()
+        while time.time() - t_soak < 1.0:   # let the sampler see the kernel under load
+            step()
+            torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = e0.elapsed_time(e1)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_max = float(t.item())
+    per_step = step_bytes(b, layers)
+    total_bytes = per_step * args.steps * world
+    value = total_bytes / (ms_max * 1e-3) / 1e12
+    launch_ms = ms / (args.steps * layers)
+    achieved_gbs = per_step / layers / (launch_ms * 1e-3) / 1e9
+    peak, peak_kind = _peaks()
+
+    # ---- e2e through the drop-in API with host buffers
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 50))
+    R, H, D = b.q.shape
+    q_host = torch.empty((layers, R, H, D), dtype=torch.float16, pin_memory=True)
+    q_host.copy_(b.q.cpu().unsqueeze(0).expand(layers, R, H, D))
+    o_host = torch.empty_like(q_host, pin_memory=True)
+    lens_host = b.seq_lens.cpu().pin_memory()
+    ids_host = b.seq_ids.cpu().pin_memory()
+    bt_host = b.block_table.cpu().pin_memory()
+    q_dev = torch.empty((layers, R, H, D), dtype=torch.float16, device=dev)
+    o_dev = torch.empty((layers, R, H * D), dtype=torch.float16, device=dev)
+    lens_dev, ids_dev, bt_dev = torch.empty_like(b.seq_lens), torch.empty_like(b.seq_ids), torch.empty_like(b.block_table)
+    from nebulasd_b200.workloads import decode_infer_state
+    st = decode_infer_state(lens_dev, ids_dev, b.seq_lens_list, b.num_kv_heads, scale)
+    mc = types.SimpleNamespace(num_q_heads=H, num_kv_heads=b.num_kv_heads, head_dim=D, num_layers=layers)
+    ec = types.SimpleNamespace(block_size=16, max_blocks_per_seq=b.block_table.shape[1])
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        lens_dev.copy_(lens_host, non_blocking=True)
+        ids_dev.copy_(ids_host, non_blocking=True)
+        bt_dev.copy_(bt_host, non_blocking=True)
+        for layer in range(layers):
+            paged_attention(q_dev[layer], b.k_cache, b.v_cache, bt_dev, mc, ec, st, layer, o_dev[layer])
+        o_host.view(layers, R, H * D).copy_(o_dev, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ems = f0.elapsed_time(f1)
+    if world > 1:
+        t = torch.tensor([ems], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e_value = per_step * e2e_steps * world / (ems * 1e-3) / 1e12
+    h2d = q_host.numel() * 2 + lens_host.numel() * 4 + ids_host.numel() * 4 + bt_host.numel() * 4
+    d2h = o_host.numel() * 2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.workload, budget_s=10.0)
+
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": args.workload, "kernel": kname, "requests_per_gpu": cfg["num_requests"],
+                   "depth": cfg["depth"], "ctx": [cfg["ctx_lo"], cfg["ctx_hi"]], "num_q_heads": cfg["num_q_heads"],
+                   "num_kv_heads": cfg["num_kv_heads"], "head_dim": 128, "block_size": 16, "num_layers": layers,
+                   "pool_blocks": cfg["pool_blocks"], "calls_per_step": layers,
+                   "l2": f"inputs larger than L2: each step streams {per_step / 1e9:.2f} GB of distinct KV",
+                   "parallelism": f"{world} independent request shards (no collective)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved_gbs / peak, 4), "peak_kind": peak_kind,
+                     "traffic": _traffic(args.workload, kname),
+                     "bytes_per_launch": per_step // layers, "launch_us": round(launch_ms * 1e3, 3)},
+        "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps, "api": "nebulasd_b200.kernels.paged_attention"},
+        "gpu_launches": args.steps * layers,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(workload: str, budget_s: float):
+    """The fp32 PyTorch-eager reference semantics on the host cores, on a bounded sample."""
+    from nebulasd_b200.workloads import CONFIGS, make_paged_batch
+    from oracle.attention import paged_attention as oracle_attention
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = dict(CONFIGS[workload])
+    cfg.pop("num_layers", None)
+    b = make_paged_batch(1234, num_layers=1, cur_layer=0, device="cpu", **cfg)
+    per_call = step_bytes(b, 1)
+    t0 = time.perf_counter()
+    calls = 0
+    while True:
+        oracle_attention(b.q, b.k_cache, b.v_cache, b.block_table, b.seq_lens_list, b.seq_ids_list, 0,
+                         b.q.shape[-1] ** -0.5)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or calls >= 200:
+            break
+    return {"value": round(per_call * calls / el / 1e12, 6), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{calls} full layer calls of {workload} (one layer, {b.num_rows} rows) "
+                                      f"in {el:.1f} s, fp32 eager oracle"}
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    from nebulasd_b200.workloads import CONFIGS, make_paged_batch
+    from oracle.attention import paged_attention as oracle_attention
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = dict(CONFIGS[args.workload])
+    cfg.pop("num_layers", None)
+    b = make_paged_batch(1234, num_layers=1, cur_layer=0, device="cpu", **cfg)
+    per_call = step_bytes(b, 1)
+    scale = b.q.shape[-1] ** -0.5
+
+    def step():
+        oracle_attention(b.q, b.k_cache, b.v_cache, b.block_table, b.seq_lens_list, b.seq_ids_list, 0, scale)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = per_call * args.steps / el / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "requests": cfg["num_requests"], "depth": cfg["depth"],
+                   "ctx": [cfg["ctx_lo"], cfg["ctx_hi"]], "num_q_heads": cfg["num_q_heads"],
+                   "num_kv_heads": cfg["num_kv_heads"], "head_dim": 128, "calls_per_step": 1},
+        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"one layer call of {args.workload} per step ({b.num_rows} rows, all requests), "
+                                   "fp32 PyTorch-eager restatement of the reference's Triton kernels"},
+        "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,181 @@
+/*
+ * nebula_b200.h -- C ABI of the B200-native swiftLLM attention hot path.
+ *
+ * Every entry point takes plain device/host pointers, sizes and a
+ * cudaStream_t passed as `void*`, launches asynchronously on that stream and
+ * returns an int status (NEB_OK = 0).  neb_last_error() gives the message of
+ * the last failure on the calling thread.  Tensors are owned by the caller.
+ *
+ * Layout contract (fixed by the reference's callers):
+ *   q / o        [num_rows, num_q_heads, head_dim]                     fp16
+ *   k/v cache    [num_blocks, num_layers, num_kv_heads, block_size, head_dim] fp16
+ *   block_table  [block_table_rows, max_blocks_per_seq]                int32
+ *   seq_lens / seq_ids  [num_rows]                                     int32
+ * head_dim must be 128 and block_size 16 (the Qwen3 / swiftLLM configuration).
+ *
+ * Reference interfaces replaced (paths relative to the NebulaSD project root):
+ *   swiftLLM/swiftllm/worker/kernels/paged_attn.py:152-222      paged_attention
+ *   swiftLLM/swiftllm/worker/kernels/kvcache_mgmt.py:81-122     store_kvcache
+ *   swiftLLM/swiftllm/worker/kernels/rotary_emb.py:44-58        rotary_embedding_inplace
+ *   swiftLLM/swiftllm/worker/kernels/rmsnorm.py:26-37           rmsnorm_inplace
+ *   nebulasd/src/nebulasd/kv/cuda_transfer.py:78-108            CudaCopyBackend.launch
+ *   swiftLLM/csrc/src/block_swapping.cpp:22-85                  swap_blocks
+ */
+#ifndef NEBULA_B200_H
+#define NEBULA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NEB_OK 0
+#define NEB_ERR_INVALID 1      /* bad argument (shape, pointer, size) */
+#define NEB_ERR_UNSUPPORTED 2  /* valid but unsupported configuration */
+#define NEB_ERR_CUDA 3         /* a CUDA runtime/driver call failed */
+#define NEB_ERR_WORKSPACE 4    /* workspace missing or too small */
+#define NEB_ERR_DEVICE 5       /* the kernel recorded an error (see neb_workspace_status) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int neb_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* neb_last_error(void);
+
+/* ------------------------------------------------------------------ attention
+ * Paged attention over decode rows.  Row r attends q[r] to the first
+ * seq_lens[r] tokens of sequence seq_ids[r]; token t of a sequence lives in
+ * cache[block_table[seq_id][t / 16], cur_layer, kv_head, t % 16, :].  Adjacent
+ * rows with the same seq_id (a verify of depth k lowers to k+1 such rows with
+ * lengths L+1..L+k+1) share one read of their KV prefix.  Output o is fp16,
+ * accumulated in fp32.  A row with seq_len <= 0 gets NaN, as the reference's
+ * 0/0 normalisation does.
+ *
+ * workspace: device scratch of at least neb_attention_workspace_bytes(...)
+ * bytes, zero-filled once before its first use and then reused by calls that
+ * are ordered on one stream (the kernels leave its counters at zero).  Calls
+ * that may overlap on the GPU need distinct workspaces.
+ *
+ * Replaces paged_attention, swiftLLM/swiftllm/worker/kernels/paged_attn.py:152-222
+ * (phase 1 :9-108, phase 2 :111-149), whose fp32 mid_o / mid_o_logexpsum
+ * buffers (:170-180) this workspace stands in for.
+ */
+#define NEB_ATTN_DECODE 0  /* CUDA-core kernel: 128-bit loads, warp shuffles */
+#define NEB_ATTN_VERIFY 1  /* tcgen05 kernel: GQA x rows packed into MMA tiles */
+
+size_t neb_attention_workspace_bytes(int kernel, int device, int num_rows, int num_q_heads,
+                                     int num_kv_heads);
+
+int neb_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache,
+                               const int32_t* block_table, int32_t block_table_rows,
+                               int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                               const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                               int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                               float softmax_scale, void* o, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Target verify attention on tcgen05 tensor cores: the GQA group and up to
+ * 64 / gqa adjacent rows of one seq_id (the k+1 verify rows) form the M
+ * dimension of one MMA tile, so each KV tile is staged once (TMA) for all of
+ * them.  Same arguments, semantics and workspace contract as the decode entry.
+ * Replaces the same reference function: paged_attn.py:152-222, as called for
+ * Target verify rows from nebulasd/src/nebulasd/workers/target/backend.py:102-111. */
+int neb_paged_attention_verify(const void* q, const void* k_cache, const void* v_cache,
+                               const int32_t* block_table, int32_t block_table_rows,
+                               int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                               const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                               int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                               float softmax_scale, void* o, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Synchronises `stream`, then reads the error bits the attention kernels
+ * recorded in `workspace` (bit 0: block index out of range, bit 1: seq_id out
+ * of range, bit 2: sequence longer than max_blocks_per_seq) and clears them. */
+int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream);
+
+/* ------------------------------------------------ QK-norm, RoPE and KV store
+ * Token layout of one forward (the reference's): prefill tokens first
+ * (sequence s occupies [prefill_start_locs[s], +prefill_seq_lens[s]) with
+ * seq_id seq_ids[s]), then num_decode_rows decode tokens (row r has seq_id
+ * seq_ids[num_prefill_seqs + r] and position decode_seq_lens[r] - 1).
+ * Out-of-range block ids / seq ids are skipped and OR-ed into *error_bits
+ * (optional device word; same bits as neb_workspace_status). */
+
+/* Fused Qwen3 QK-RMSNorm + RoPE + paged KV store, in one launch:
+ *   q, k <- RoPE(RMSNorm(x) rounded to fp16)   (in place; norm skipped when the
+ *                                               weights are null, RoPE when cos is null)
+ *   k_cache/v_cache[slot(token)] <- k, v       (skipped when k_cache is null)
+ * Replaces the call sequence swiftLLM/swiftllm/worker/layers/transformer_layer.py:114-143
+ * (rmsnorm_inplace x2 rmsnorm.py:26-37, rotary_embedding_inplace rotary_emb.py:44-58,
+ * store_kvcache kvcache_mgmt.py:81-122). */
+int neb_qk_norm_rope_store(void* q, void* k, const void* v, const void* q_norm_w,
+                           const void* k_norm_w, float eps, const void* cos, const void* sin,
+                           void* k_cache, void* v_cache, const int32_t* block_table,
+                           int32_t block_table_rows, int32_t max_blocks_per_seq,
+                           const int32_t* seq_ids, const int32_t* decode_seq_lens,
+                           int32_t num_decode_rows, const int32_t* prefill_start_locs,
+                           const int32_t* prefill_seq_lens, int32_t num_prefill_seqs,
+                           int32_t num_prefill_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                           int32_t head_dim, int32_t block_size, int64_t num_blocks,
+                           int32_t num_layers, int32_t cur_layer, uint32_t* error_bits,
+                           void* stream);
+
+/* Paged KV store only (bit copies).  Replaces store_kvcache,
+ * swiftLLM/swiftllm/worker/kernels/kvcache_mgmt.py:81-122 (kernels :10-79). */
+int neb_store_kvcache(const void* k, const void* v, void* k_cache, void* v_cache,
+                      const int32_t* block_table, int32_t block_table_rows,
+                      int32_t max_blocks_per_seq, const int32_t* seq_ids,
+                      const int32_t* decode_seq_lens, int32_t num_decode_rows,
+                      const int32_t* prefill_start_locs, const int32_t* prefill_seq_lens,
+                      int32_t num_prefill_seqs, int32_t num_prefill_tokens, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t block_size, int64_t num_blocks, int32_t num_layers,
+                      int32_t cur_layer, uint32_t* error_bits, void* stream);
+
+/* In-place RMSNorm of num_rows rows of `hidden` fp16 values.  Replaces
+ * rmsnorm_inplace, swiftLLM/swiftllm/worker/kernels/rmsnorm.py:26-37. */
+int neb_rmsnorm_inplace(void* x, const void* weight, int64_t num_rows, int32_t hidden, float eps,
+                        void* stream);
+
+/* In-place rotate-half RoPE of q [T, Hq, 128] and k [T, Hk, 128] with fp16
+ * cos/sin rows [T, 64], in the reference's fp16 arithmetic.  Replaces
+ * rotary_embedding_inplace, swiftLLM/swiftllm/worker/kernels/rotary_emb.py:44-58. */
+int neb_rotary_inplace(void* q, void* k, const void* cos, const void* sin, int32_t num_tokens,
+                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, void* stream);
+
+/* ------------------------------------------------------------ HostKV copies
+ * direction 0 = D2H (writeback), 1 = H2D (restore).  regions: host array of
+ * num_regions triples (host_block, gpu_block, block_count), host_block
+ * already including the extent offset; each block moves block_bytes bytes of
+ * the K plane and of the V plane.  Destination ranges must not overlap.
+ * mode 0: one cudaMemcpyAsync per merged run of adjacent regions and plane;
+ * mode 1: one copy kernel for the whole plan (host planes must be pinned and
+ * mapped; pass their device addresses, see neb_host_device_pointer).
+ * Replaces CudaCopyBackend.launch, nebulasd/src/nebulasd/kv/cuda_transfer.py:78-108,
+ * and swap_blocks, swiftLLM/csrc/src/block_swapping.cpp:22-85. */
+int neb_hostkv_copy(int direction, const void* host_k_plane, const void* host_v_plane,
+                    void* k_cache, void* v_cache, int64_t block_bytes, const int64_t* regions,
+                    int32_t num_regions, int32_t mode, void* stream);
+
+/* Same-role KV migration as a direct GPU-to-GPU copy: regions are triples
+ * (src_block, dst_block, block_count) between two caches of one layout; run
+ * on the destination device (mode 1 reads the peer cache from a kernel over
+ * NVLink; enable access first with neb_enable_peer_access).  Replaces the
+ * writeback + restore through HostKV of nebulasd/docs/current/KV.md:3-22. */
+int neb_kv_peer_copy(const void* src_k_cache, const void* src_v_cache, void* dst_k_cache,
+                     void* dst_v_cache, int64_t block_bytes, const int64_t* regions,
+                     int32_t num_regions, int32_t mode, void* stream);
+
+/* Device address of pinned, mapped host memory (cudaHostGetDevicePointer). */
+int neb_host_device_pointer(void* host_ptr, void** device_ptr);
+
+/* Lets the current device read `peer_device`'s memory (idempotent). */
+int neb_enable_peer_access(int peer_device);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NEBULA_B200_H */

@@ -1,0 +1,212 @@
+// C ABI: argument validation, workspace sizing and dispatch of the attention kernels.
+#include <cstdarg>
+#include <cstring>
+
+#include "attn_common.cuh"
+
+namespace neb {
+
+static thread_local char g_last_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  return set_error(NEB_ERR_CUDA, "%s failed: %s (%d)", what, cudaGetErrorString(e), (int)e);
+}
+
+int num_sms(int device) {
+  static int cache[64] = {};
+  if (device < 0 || device >= 64) return 0;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+long long decode_workers(int device, int gqa);
+int launch_decode(const AttnParams& p, long long workers, cudaStream_t stream);
+long long verify_workers(int device);
+int verify_group_rows(int gqa);
+int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream);
+
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Validates the common attention arguments and fills everything but the workspace.
+static int attention_params(AttnParams& p, const void* q, const void* k_cache, const void* v_cache,
+                            const int32_t* block_table, int32_t block_table_rows,
+                            int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                            const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                            int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                            int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                            float softmax_scale, void* o) {
+  NEB_REQUIRE(head_dim == kHeadDim, NEB_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  NEB_REQUIRE(block_size == kBlockTokens, NEB_ERR_UNSUPPORTED, "block_size must be 16 (got %d)", block_size);
+  NEB_REQUIRE(num_rows >= 0 && num_rows <= kMaxRows, NEB_ERR_UNSUPPORTED,
+              "num_rows must be in [0, %d] (got %d)", kMaxRows, num_rows);
+  NEB_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
+              NEB_ERR_INVALID, "num_q_heads (%d) must be a positive multiple of num_kv_heads (%d)",
+              num_q_heads, num_kv_heads);
+  NEB_REQUIRE(num_layers > 0 && cur_layer >= 0 && cur_layer < num_layers, NEB_ERR_INVALID,
+              "cur_layer %d outside [0, %d)", cur_layer, num_layers);
+  NEB_REQUIRE(num_blocks > 0 && block_table_rows > 0 && max_blocks_per_seq > 0, NEB_ERR_INVALID,
+              "num_blocks, block_table_rows and max_blocks_per_seq must be positive");
+  NEB_REQUIRE(q && k_cache && v_cache && block_table && seq_lens && seq_ids && o, NEB_ERR_INVALID,
+              "null tensor pointer");
+  NEB_REQUIRE(aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(o),
+              NEB_ERR_INVALID, "q, caches and o must be 16-byte aligned");
+  NEB_REQUIRE(softmax_scale > 0.f, NEB_ERR_INVALID, "softmax_scale must be positive");
+  std::memset(&p, 0, sizeof(p));
+  p.q = static_cast<const __half*>(q);
+  p.k_cache = static_cast<const __half*>(k_cache);
+  p.v_cache = static_cast<const __half*>(v_cache);
+  p.block_table = block_table;
+  p.bt_rows = block_table_rows;
+  p.mbs = max_blocks_per_seq;
+  p.seq_lens = seq_lens;
+  p.seq_ids = seq_ids;
+  p.num_rows = num_rows;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.num_blocks = num_blocks;
+  p.num_layers = num_layers;
+  p.cur_layer = cur_layer;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.o = static_cast<__half*>(o);
+  return NEB_OK;
+}
+
+static int bind_workspace(AttnParams& p, void* workspace, size_t workspace_bytes, long long workers,
+                          int nq) {
+  const WorkspaceLayout L = workspace_layout(workers, p.num_rows, p.num_kv_heads, nq);
+  NEB_REQUIRE(workspace != nullptr, NEB_ERR_WORKSPACE, "workspace is null");
+  NEB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, NEB_ERR_WORKSPACE,
+              "workspace must be 256-byte aligned");
+  NEB_REQUIRE(workspace_bytes >= L.total, NEB_ERR_WORKSPACE,
+              "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, L.total);
+  char* base = static_cast<char*>(workspace);
+  p.hdr = reinterpret_cast<WorkspaceHeader*>(base);
+  p.counters = reinterpret_cast<int32_t*>(base + L.counters);
+  p.part_lse = reinterpret_cast<float*>(base + L.part_lse);
+  p.part_o = reinterpret_cast<float*>(base + L.part_o);
+  p.nq = nq;
+  return NEB_OK;
+}
+
+static int attention_workers(int kernel, int device, int gqa, long long* workers, int* nq,
+                             int* group_rows) {
+  if (kernel == NEB_ATTN_DECODE) {
+    NEB_REQUIRE(gqa == 1 || gqa == 2 || gqa == 4 || gqa == 8, NEB_ERR_UNSUPPORTED,
+                "decode attention supports q/kv head ratios 1, 2, 4, 8 (got %d)", gqa);
+    *workers = decode_workers(device, gqa);
+    *group_rows = 1;
+  } else if (kernel == NEB_ATTN_VERIFY) {
+    *group_rows = verify_group_rows(gqa);
+    NEB_REQUIRE(*group_rows > 0, NEB_ERR_UNSUPPORTED,
+                "verify attention supports q/kv head ratios 1..16 (got %d)", gqa);
+    *workers = verify_workers(device);
+  } else {
+    return set_error(NEB_ERR_INVALID, "unknown attention kernel %d", kernel);
+  }
+  NEB_REQUIRE(*workers > 0, NEB_ERR_CUDA, "could not size the grid for device %d", device);
+  *nq = gqa * *group_rows;
+  return NEB_OK;
+}
+
+}  // namespace neb
+
+using namespace neb;
+
+extern "C" {
+
+int neb_version(void) { return 100; }
+
+const char* neb_last_error(void) { return g_last_error; }
+
+size_t neb_attention_workspace_bytes(int kernel, int device, int num_rows, int num_q_heads,
+                                     int num_kv_heads) {
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || num_rows < 0) return 0;
+  long long workers = 0;
+  int nq = 0, group_rows = 0;
+  if (attention_workers(kernel, device, num_q_heads / num_kv_heads, &workers, &nq, &group_rows) != NEB_OK)
+    return 0;
+  return workspace_layout(workers, num_rows > 0 ? num_rows : 1, num_kv_heads, nq).total;
+}
+
+static int paged_attention_impl(int kernel, const void* q, const void* k_cache, const void* v_cache,
+                                const int32_t* block_table, int32_t block_table_rows,
+                                int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                                const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                                float softmax_scale, void* o, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  AttnParams p;
+  int rc = attention_params(p, q, k_cache, v_cache, block_table, block_table_rows, max_blocks_per_seq,
+                            seq_lens, seq_ids, num_rows, num_q_heads, num_kv_heads, head_dim,
+                            block_size, num_blocks, num_layers, cur_layer, softmax_scale, o);
+  if (rc != NEB_OK) return rc;
+  if (num_rows == 0) return NEB_OK;
+  int device = 0;
+  NEB_CUDA(cudaGetDevice(&device));
+  long long workers = 0;
+  int nq = 0, group_rows = 0;
+  rc = attention_workers(kernel, device, num_q_heads / num_kv_heads, &workers, &nq, &group_rows);
+  if (rc != NEB_OK) return rc;
+  rc = bind_workspace(p, workspace, workspace_bytes, workers, nq);
+  if (rc != NEB_OK) return rc;
+  p.max_group_rows = group_rows;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return kernel == NEB_ATTN_DECODE ? launch_decode(p, workers, s) : launch_verify(p, workers, s);
+}
+
+int neb_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache,
+                               const int32_t* block_table, int32_t block_table_rows,
+                               int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                               const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                               int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                               float softmax_scale, void* o, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  return paged_attention_impl(NEB_ATTN_DECODE, q, k_cache, v_cache, block_table, block_table_rows,
+                              max_blocks_per_seq, seq_lens, seq_ids, num_rows, num_q_heads,
+                              num_kv_heads, head_dim, block_size, num_blocks, num_layers, cur_layer,
+                              softmax_scale, o, workspace, workspace_bytes, stream);
+}
+
+int neb_paged_attention_verify(const void* q, const void* k_cache, const void* v_cache,
+                               const int32_t* block_table, int32_t block_table_rows,
+                               int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                               const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                               int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                               float softmax_scale, void* o, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  return paged_attention_impl(NEB_ATTN_VERIFY, q, k_cache, v_cache, block_table, block_table_rows,
+                              max_blocks_per_seq, seq_lens, seq_ids, num_rows, num_q_heads,
+                              num_kv_heads, head_dim, block_size, num_blocks, num_layers, cur_layer,
+                              softmax_scale, o, workspace, workspace_bytes, stream);
+}
+
+int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream) {
+  NEB_REQUIRE(workspace && error_bits, NEB_ERR_INVALID, "null argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  WorkspaceHeader h;
+  NEB_CUDA(cudaMemcpyAsync(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost, s));
+  NEB_CUDA(cudaStreamSynchronize(s));
+  *error_bits = h.error_bits;
+  if (h.error_bits) {
+    NEB_CUDA(cudaMemsetAsync(workspace, 0, sizeof(uint32_t), s));
+    NEB_CUDA(cudaStreamSynchronize(s));
+  }
+  return NEB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,112 @@
+"""Paged decode / verify attention behind the reference's ``paged_attention`` signature.
+
+Replaces ``swiftLLM/swiftllm/worker/kernels/paged_attn.py:152-222``.  Same
+arguments, same contiguity assertions (``:163-168``), same outputs written into
+``o``; one launch instead of two, no per-call ``torch.empty`` of partials.
+
+Two CUDA kernels implement it (both correct for any row layout):
+  * ``decode``: CUDA cores, for the Draft's single-token rows;
+  * ``verify``: tcgen05 tensor cores, packing the GQA group and the k+1
+    speculative rows of one request into the M dimension of the MMA tile.
+``NEB_PAGED_ATTENTION=decode|verify|auto`` (or ``set_kernel``) picks one; ``auto``
+uses ``verify`` when the q/kv head ratio is 4 or more (the Qwen3-8B Target)
+and ``decode`` otherwise (the Qwen3-0.6B Draft), when both are built.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from .. import _lib
+from .._workspace import attention_workspace
+
+_MODES = {"auto": None, "decode": _lib.NEB_ATTN_DECODE, "verify": _lib.NEB_ATTN_VERIFY}
+_mode = os.environ.get("NEB_PAGED_ATTENTION", "auto").lower()
+if _mode not in _MODES:
+    raise ValueError(f"NEB_PAGED_ATTENTION must be one of {sorted(_MODES)} (got {_mode!r})")
+
+
+def set_kernel(mode: str) -> None:
+    """Select ``"auto"``, ``"decode"`` or ``"verify"`` for later calls."""
+    global _mode
+    if mode not in _MODES:
+        raise ValueError(f"kernel must be one of {sorted(_MODES)}")
+    _mode = mode
+
+
+def get_kernel() -> str:
+    return _mode
+
+
+VERIFY_BUILT = os.environ.get("NEB_VERIFY_BUILT", "0") == "1"
+
+
+def choose_kernel(num_q_heads: int, num_kv_heads: int) -> int:
+    forced = _MODES[_mode]
+    if forced is not None:
+        return forced
+    if VERIFY_BUILT and num_q_heads // num_kv_heads >= 4:
+        return _lib.NEB_ATTN_VERIFY
+    return _lib.NEB_ATTN_DECODE
+
+
+def _check_tensors(q, k_cache, v_cache, block_table, seq_lens, seq_ids, o):
+    if q.dtype != torch.float16 or k_cache.dtype != torch.float16 or v_cache.dtype != torch.float16 \
+            or o.dtype != torch.float16:
+        raise TypeError("q, k_cache, v_cache and o must be float16")
+    if block_table.dtype != torch.int32 or seq_lens.dtype != torch.int32 or seq_ids.dtype != torch.int32:
+        raise TypeError("block_table, seq_lens and seq_ids must be int32")
+    dev = q.device
+    if dev.type != "cuda" or any(t.device != dev for t in (k_cache, v_cache, block_table, seq_lens, seq_ids, o)):
+        raise ValueError("all tensors must be on the same CUDA device")
+    if k_cache.shape != v_cache.shape or k_cache.dim() != 5:
+        raise ValueError("k_cache/v_cache must be [num_blocks, num_layers, num_kv_heads, block_size, head_dim]")
+    if not (seq_lens.is_contiguous() and seq_ids.is_contiguous()):
+        raise ValueError("seq_lens and seq_ids must be contiguous")
+
+
+def paged_attention_raw(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                        block_table: torch.Tensor, seq_lens: torch.Tensor, seq_ids: torch.Tensor,
+                        cur_layer: int, softmax_scale: float, o: torch.Tensor,
+                        kernel: int | None = None, workspace: torch.Tensor | None = None,
+                        stream: torch.cuda.Stream | None = None) -> None:
+    """Tensor-level entry: ``o[r] = attention(q[r], KV of seq_ids[r] up to seq_lens[r])``."""
+    _check_tensors(q, k_cache, v_cache, block_table, seq_lens, seq_ids, o)
+    num_rows, num_q_heads, head_dim = q.shape
+    num_blocks, num_layers, num_kv_heads, block_size, _ = k_cache.shape
+    if o.shape != q.shape or seq_lens.shape[0] != num_rows or seq_ids.shape[0] != num_rows:
+        raise ValueError("q, o, seq_lens and seq_ids disagree on the number of rows")
+    if kernel is None:
+        kernel = choose_kernel(num_q_heads, num_kv_heads)
+    stream = stream or torch.cuda.current_stream(q.device)
+    if workspace is None:
+        workspace = attention_workspace(kernel, q.device, stream, num_rows, num_q_heads, num_kv_heads)
+    fn = _lib.lib.neb_paged_attention_verify if kernel == _lib.NEB_ATTN_VERIFY else _lib.lib.neb_paged_attention_decode
+    rc = fn(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
+            block_table.shape[0], block_table.shape[1], seq_lens.data_ptr(), seq_ids.data_ptr(),
+            num_rows, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks, num_layers,
+            cur_layer, float(softmax_scale), o.data_ptr(), workspace.data_ptr(), workspace.numel(),
+            stream.cuda_stream)
+    _lib.check(rc, "paged_attention")
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    block_table: torch.Tensor, model_config, engine_config, infer_state,
+                    cur_layer: int, o: torch.Tensor) -> None:
+    """Drop-in for the reference's ``paged_attention`` (same signature and asserts)."""
+    assert q.is_contiguous()
+    assert k_cache.is_contiguous()
+    assert v_cache.is_contiguous()
+    assert block_table.is_contiguous()
+    assert infer_state.seq_block_size % engine_config.block_size == 0
+    assert o.is_contiguous()
+    if infer_state.num_decoding_seqs == 0:
+        return
+    if block_table.shape[1] != engine_config.max_blocks_per_seq:
+        raise ValueError("block_table.shape[1] must equal engine_config.max_blocks_per_seq")
+    o3 = o.view(infer_state.num_decoding_seqs, model_config.num_q_heads, model_config.head_dim)
+    q3 = q.view(infer_state.num_decoding_seqs, model_config.num_q_heads, model_config.head_dim)
+    paged_attention_raw(q3, k_cache, v_cache, block_table, infer_state.decoding_seq_lens,
+                        infer_state.seq_ids[infer_state.num_prefill_seqs:], cur_layer,
+                        infer_state.softmax_scale, o3)

@@ -1,0 +1,92 @@
+"""CPU: the C-ABI library loads, exports every declared symbol and validates arguments."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "nebula_b200.h"
+
+
+def declared_symbols():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(neb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_hot_path():
+    names = declared_symbols()
+    for must in ("neb_paged_attention_decode", "neb_paged_attention_verify", "neb_store_kvcache",
+                 "neb_qk_norm_rope_store", "neb_rotary_inplace", "neb_rmsnorm_inplace", "neb_hostkv_copy",
+                 "neb_kv_peer_copy"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from nebulasd_b200 import _lib
+    for name in declared_symbols():
+        assert hasattr(_lib.lib, name), f"{name} declared in the header but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version_and_empty_error():
+    from nebulasd_b200 import _lib
+    assert _lib.lib.neb_version() >= 100
+    assert isinstance(_lib.lib.neb_last_error(), bytes)
+
+
+def _attn_args(**kw):
+    a = dict(q=16, k=16, v=16, bt=16, bt_rows=4, mbs=8, lens=16, ids=16, rows=2, h=16, hk=8, d=128, bs=16,
+             nb=64, layers=1, layer=0, scale=0.088, o=16, ws=256, wsb=1 << 20, stream=None)
+    a.update(kw)
+    return list(a.values())
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(d=64), b"head_dim must be 128"),
+    (dict(bs=32), b"block_size must be 16"),
+    (dict(h=12, hk=8), b"multiple of num_kv_heads"),
+    (dict(layer=3, layers=2), b"cur_layer 3 outside"),
+    (dict(rows=5000), b"num_rows must be in"),
+    (dict(q=None), b"null tensor pointer"),
+    (dict(q=8), b"16-byte aligned"),
+    (dict(scale=0.0), b"softmax_scale must be positive"),
+])
+def test_attention_argument_validation_without_gpu(kw, msg):
+    from nebulasd_b200 import _lib
+    for fn in (_lib.lib.neb_paged_attention_decode, _lib.lib.neb_paged_attention_verify):
+        rc = fn(*_attn_args(**kw))
+        assert rc == 1 or rc == 2
+        assert msg in _lib.lib.neb_last_error()
+
+
+def test_zero_rows_is_a_no_op():
+    from nebulasd_b200 import _lib
+    assert _lib.lib.neb_paged_attention_decode(*_attn_args(rows=0)) == 0
+
+
+def test_copy_validation_rejects_overlap_and_negative_ranges():
+    from nebulasd_b200 import _lib
+    import numpy as np
+    regions = np.array([[0, 0, 4], [8, 2, 4]], dtype=np.int64)
+    rc = _lib.lib.neb_hostkv_copy(1, 16, 16, 16, 16, 4096, regions.ctypes.data, 2, 0, None)
+    assert rc == 1 and b"overlap" in _lib.lib.neb_last_error()
+    regions = np.array([[0, -1, 4]], dtype=np.int64)
+    rc = _lib.lib.neb_hostkv_copy(1, 16, 16, 16, 16, 4096, regions.ctypes.data, 1, 0, None)
+    assert rc == 1 and b"negative" in _lib.lib.neb_last_error()
+    rc = _lib.lib.neb_hostkv_copy(1, 16, 16, 16, 16, 4095, regions.ctypes.data, 1, 0, None)
+    assert rc == 1 and b"multiple of 16" in _lib.lib.neb_last_error()
+
+
+def test_store_and_rope_validation_without_gpu():
+    from nebulasd_b200 import _lib
+    rc = _lib.lib.neb_rotary_inplace(8, 8, 8, 8, 1, 4, 2, 64, None)
+    assert rc == 2 and b"head_dim must be 128" in _lib.lib.neb_last_error()
+    rc = _lib.lib.neb_rmsnorm_inplace(None, 8, 1, 128, 1e-6, None)
+    assert rc == 1
+
+
+def test_op_modules_import_without_gpu():
+    import nebulasd_b200
+    from nebulasd_b200 import kernels, hostkv  # noqa: F401
+    assert callable(kernels.paged_attention) and callable(nebulasd_b200.install)
