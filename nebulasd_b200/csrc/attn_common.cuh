@@ -36,6 +36,11 @@ struct AttnParams {
 };
 
 // Workspace: header | counters | part_lse | part_o, each 256-byte aligned.
+// The counter region has a fixed size and place whatever the call's shape, so
+// the partials of one call can never land where a later call (with more rows
+// or heads) keeps counters that must read zero.
+constexpr int kMaxKvHeads = 64;
+
 struct WorkspaceLayout {
   size_t counters, part_lse, part_o, total;
 };
@@ -44,9 +49,11 @@ __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_
 
 __host__ __device__ inline WorkspaceLayout workspace_layout(long long workers, int num_rows,
                                                             int num_kv_heads, int nq) {
+  (void)num_rows;
+  (void)num_kv_heads;
   WorkspaceLayout L;
   L.counters = sizeof(WorkspaceHeader);
-  L.part_lse = L.counters + align256((size_t)num_rows * num_kv_heads * sizeof(int32_t));
+  L.part_lse = L.counters + align256((size_t)kMaxRows * kMaxKvHeads * sizeof(int32_t));
   L.part_o = L.part_lse + align256((size_t)2 * workers * nq * sizeof(float));
   L.total = L.part_o + align256((size_t)2 * workers * nq * kHeadDim * sizeof(float));
   return L;

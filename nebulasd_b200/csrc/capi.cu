@@ -51,6 +51,8 @@ static int attention_params(AttnParams& p, const void* q, const void* k_cache, c
   NEB_REQUIRE(block_size == kBlockTokens, NEB_ERR_UNSUPPORTED, "block_size must be 16 (got %d)", block_size);
   NEB_REQUIRE(num_rows >= 0 && num_rows <= kMaxRows, NEB_ERR_UNSUPPORTED,
               "num_rows must be in [0, %d] (got %d)", kMaxRows, num_rows);
+  NEB_REQUIRE(num_kv_heads > 0 && num_kv_heads <= kMaxKvHeads, NEB_ERR_UNSUPPORTED,
+              "num_kv_heads must be in [1, %d] (got %d)", kMaxKvHeads, num_kv_heads);
   NEB_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
               NEB_ERR_INVALID, "num_q_heads (%d) must be a positive multiple of num_kv_heads (%d)",
               num_q_heads, num_kv_heads);
@@ -132,7 +134,9 @@ const char* neb_last_error(void) { return g_last_error; }
 
 size_t neb_attention_workspace_bytes(int kernel, int device, int num_rows, int num_q_heads,
                                      int num_kv_heads) {
-  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || num_rows < 0) return 0;
+  if (num_kv_heads <= 0 || num_kv_heads > kMaxKvHeads || num_q_heads <= 0 || num_q_heads % num_kv_heads ||
+      num_rows < 0)
+    return 0;
   long long workers = 0;
   int nq = 0, group_rows = 0;
   if (attention_workers(kernel, device, num_q_heads / num_kv_heads, &workers, &nq, &group_rows) != NEB_OK)

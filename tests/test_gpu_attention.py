@@ -166,3 +166,17 @@ def test_target_verify_full_size_property(kernel, cuda):
         ref = oracle.paged_attention(b.q[rows].cpu(), kc, vc, bt, [b.seq_lens_list[i] for i in rows],
                                      [0] * len(rows), 0, 128 ** -0.5)
         torch.testing.assert_close(o[rows].float().cpu(), ref, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_counters_return_to_zero_across_shapes(kernel, cuda):
+    """Every call leaves the workspace's arrival counters at zero, whatever the next call's shape."""
+    from nebulasd_b200._workspace import attention_workspace
+    stream = torch.cuda.current_stream(cuda)
+    ws = attention_workspace(_kernel_id(kernel), cuda, stream, 4096, 32, 8)
+    counters = ws[256:256 + 4096 * 64 * 4]
+    for i, shape in enumerate(["verify_deep", "decode_gqa2", "verify_gqa4_k4", "verify_gqa4_ragged", "gqa8"]):
+        c = batch_case(50 + i, **SHAPES[shape])
+        out = run_attention(c, kernel, cuda, workspace=ws)
+        assert int(torch.count_nonzero(counters).item()) == 0, f"stale counters after {shape}"
+        torch.testing.assert_close(out, oracle_of(c), atol=ATOL, rtol=RTOL)
