@@ -92,6 +92,30 @@ int neb_paged_attention_verify(const void* q, const void* k_cache, const void* v
                                float softmax_scale, void* o, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* Decode attention that allocates nothing.  It has no counterpart in the
+ * reference.  Some callers cannot call cudaMalloc: a worker whose device
+ * memory was claimed up front by its KV-cache pool (swiftLLM sizes the pool
+ * from the free memory left after profiling), a host that forbids calls which
+ * may synchronise the device while copies and compute overlap on other
+ * streams, or an FFI host with no device allocator of its own.  This entry
+ * takes the same arguments as neb_paged_attention_decode minus the workspace:
+ * its split-K scratch is a 16 MiB static __device__ array inside this library
+ * (held on every GPU that loads the library until the process exits).  Calls
+ * needing more scratch than that (more SMs or a larger q/kv head ratio than a
+ * B200 at ratio 8) fail with NEB_ERR_WORKSPACE.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current, so make that first call before any stream capture.  Every call
+ * clears the scratch it needs to start at zero, on `stream`, and allocates
+ * nothing.  All calls share the one array: calls that may overlap on the GPU
+ * (different streams without ordering between them) race and must not be made. */
+int neb_paged_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                       const int32_t* block_table, int32_t block_table_rows,
+                                       int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                                       const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                                       int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                       int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                                       float softmax_scale, void* o, void* stream);
+
 /* Synchronises `stream`, then reads the error bits the attention kernels
  * recorded in `workspace` (bit 0: block index out of range, bit 1: seq_id out
  * of range, bit 2: sequence longer than max_blocks_per_seq) and clears them. */

@@ -214,3 +214,72 @@ int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------- allocation-free decode attention
+// For callers that cannot allocate device memory: the split-K scratch of the
+// decode kernel lives in one statically sized __device__ array of this
+// library instead of a caller-provided workspace.  See the declaration of
+// neb_paged_attention_decode_noalloc in include/nebula_b200.h for the contract.
+#include <mutex>
+
+namespace neb {
+
+// Holds the header, the arrival counters and the partials of one decode call
+// on a B200 (148 SMs): at most about 11 MiB for q/kv head ratios up to 8.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mutex;
+static void* g_noalloc_address[64] = {};
+
+// Device address of the static scratch on `device`, which must be current.
+// In host code `g_noalloc_scratch` names a host-side stand-in, not device
+// memory, so the address is looked up once per device and kept.
+static int noalloc_scratch_address(int device, void** address) {
+  NEB_REQUIRE(device >= 0 && device < 64, NEB_ERR_UNSUPPORTED, "device index %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_address[device] == nullptr) {
+    void* ptr = nullptr;
+    NEB_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    g_noalloc_address[device] = ptr;
+  }
+  *address = g_noalloc_address[device];
+  return NEB_OK;
+}
+
+}  // namespace neb
+
+extern "C" int neb_paged_attention_decode_noalloc(
+    const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+    int32_t block_table_rows, int32_t max_blocks_per_seq, const int32_t* seq_lens, const int32_t* seq_ids,
+    int32_t num_rows, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int64_t num_blocks, int32_t num_layers, int32_t cur_layer, float softmax_scale, void* o, void* stream) {
+  AttnParams p;
+  int rc = attention_params(p, q, k_cache, v_cache, block_table, block_table_rows, max_blocks_per_seq,
+                            seq_lens, seq_ids, num_rows, num_q_heads, num_kv_heads, head_dim, block_size,
+                            num_blocks, num_layers, cur_layer, softmax_scale, o);
+  if (rc != NEB_OK) return rc;
+  if (num_rows == 0) return NEB_OK;
+  int device = 0;
+  NEB_CUDA(cudaGetDevice(&device));
+  long long workers = 0;
+  int nq = 0, group_rows = 0;
+  rc = attention_workers(NEB_ATTN_DECODE, device, num_q_heads / num_kv_heads, &workers, &nq, &group_rows);
+  if (rc != NEB_OK) return rc;
+  const WorkspaceLayout L = workspace_layout(workers, num_rows, num_kv_heads, nq);
+  NEB_REQUIRE(L.total <= kNoAllocScratchBytes, NEB_ERR_WORKSPACE,
+              "this call needs %zu bytes of scratch; the static scratch holds %zu", L.total,
+              kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  rc = noalloc_scratch_address(device, &scratch);
+  if (rc != NEB_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's bytes.  The header and the counters
+  // this call can touch must start at zero; the partials are written before
+  // they are read.
+  NEB_CUDA(cudaMemsetAsync(scratch, 0, L.counters + (size_t)num_rows * num_kv_heads * sizeof(int32_t), s));
+  rc = bind_workspace(p, scratch, kNoAllocScratchBytes, workers, nq);
+  if (rc != NEB_OK) return rc;
+  p.max_group_rows = group_rows;
+  return launch_decode(p, workers, s);
+}
