@@ -54,6 +54,9 @@ def _args():
     ap.add_argument("--kernel", default="auto", choices=("auto", "decode", "verify"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override the workload's layer count (profiling: a small pool, same per-call shape)")
+    ap.add_argument("--no-soak", action="store_true", help="skip the 1 s clock-sampling soak (profiling runs)")
     return ap.parse_args()
 
 
@@ -138,10 +141,12 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_workload(name: str, seed: int, device):
+def build_workload(name: str, seed: int, device, layers_override=None):
     from nebulasd_b200.workloads import CONFIGS, make_paged_batch
     cfg = dict(CONFIGS[name])
     layers = cfg.pop("num_layers", 1)
+    if layers_override:
+        layers = layers_override
     b = make_paged_batch(seed, num_layers=layers, cur_layer=0, device=device, **cfg)
     return b, layers, cfg
 
@@ -166,7 +171,7 @@ def run_ours(args):
     from nebulasd_b200.kernels.paged_attn import choose_kernel, set_kernel
     set_kernel(args.kernel)
 
-    b, layers, cfg = build_workload(args.workload, 1234 + 7919 * rank, dev)
+    b, layers, cfg = build_workload(args.workload, 1234 + 7919 * rank, dev, args.layers)
     kernel = choose_kernel(b.num_q_heads, b.num_kv_heads)
     kname = "verify" if kernel == _lib.NEB_ATTN_VERIFY else "decode"
     o = torch.empty_like(b.q)
@@ -187,7 +192,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     with Clocks(local) as clk:
         t_soak = time.time()
-        while time.time() - t_soak < 1.0:   # let the sampler see the kernel under load
+        while not args.no_soak and time.time() - t_soak < 1.0:   # let the sampler see the kernel under load
             step()
             torch.cuda.synchronize()
         barrier()

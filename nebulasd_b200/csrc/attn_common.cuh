@@ -89,11 +89,12 @@ __device__ __forceinline__ long long tile_offset(const AttnParams& p, long long 
 // kv_head * gqa + g.  Pieces whose lse is -inf (no unmasked token) carry no
 // weight; if every piece is empty the result is 0/0 = NaN, as in the
 // reference's phase 2 (swiftLLM/swiftllm/worker/kernels/paged_attn.py:131-149).
+// The warp handles unit rows jbegin, jbegin + jstep, ...
 __device__ inline void merge_unit_warp(const AttnParams& p, int first_row, int nrows, int kv_head,
-                                       int gqa, long long w0, long long w1) {
+                                       int gqa, long long w0, long long w1, int jbegin = 0, int jstep = 1) {
   const int lane = threadIdx.x & 31;
   const int nqu = nrows * gqa;
-  for (int j = 0; j < nqu; ++j) {
+  for (int j = jbegin; j < nqu; j += jstep) {
     float mx = neg_inf();
     for (long long w = w0; w <= w1; ++w) {
       const long long slot = piece_slot(w, w0);

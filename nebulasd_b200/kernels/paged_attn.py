@@ -39,7 +39,7 @@ def get_kernel() -> str:
     return _mode
 
 
-VERIFY_BUILT = os.environ.get("NEB_VERIFY_BUILT", "0") == "1"
+VERIFY_BUILT = os.environ.get("NEB_VERIFY_BUILT", "1") == "1"
 
 
 def choose_kernel(num_q_heads: int, num_kv_heads: int) -> int:

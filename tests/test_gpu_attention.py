@@ -68,8 +68,8 @@ SHAPES = {
     # k=8 and ragged depths, shuffled table rows
     "verify_gqa4_ragged": dict(num_requests=7, depth=[8, 0, 3, 8, 1, 5, 2], ctx_lo=1, ctx_hi=900,
                                num_q_heads=32, num_kv_heads=8, pool_blocks=600, shuffle_seq_ids=True),
-    # group longer than one MMA tile can hold (depth 20 -> 21 rows x GQA 4 > 64)
-    "verify_deep": dict(num_requests=2, depth=20, ctx_lo=50, ctx_hi=300, num_q_heads=32, num_kv_heads=8,
+    # group longer than one MMA tile can hold (depth 40 -> 41 rows x GQA 4 > 128)
+    "verify_deep": dict(num_requests=2, depth=40, ctx_lo=50, ctx_hi=300, num_q_heads=32, num_kv_heads=8,
                         pool_blocks=64),
     # GQA 1 and GQA 8
     "mha": dict(num_requests=5, depth=2, ctx_lo=10, ctx_hi=400, num_q_heads=4, num_kv_heads=4, pool_blocks=200),
