@@ -172,7 +172,7 @@ def run_ours(args):
     set_kernel(args.kernel)
 
     b, layers, cfg = build_workload(args.workload, 1234 + 7919 * rank, dev, args.layers)
-    kernel = choose_kernel(b.num_q_heads, b.num_kv_heads)
+    kernel = choose_kernel(b.num_q_heads, b.num_kv_heads, int(b.q.shape[0]))
     kname = "verify" if kernel == _lib.NEB_ATTN_VERIFY else "decode"
     o = torch.empty_like(b.q)
     stream = torch.cuda.current_stream(dev)

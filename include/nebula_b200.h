@@ -68,6 +68,11 @@ const char* neb_last_error(void);
 size_t neb_attention_workspace_bytes(int kernel, int device, int num_rows, int num_q_heads,
                                      int num_kv_heads);
 
+/* Largest num_rows one call of `kernel` accepts (the plan of a call lives in
+ * shared memory); larger batches are split by the caller or go to the other
+ * kernel.  The reference has no such bound. */
+int neb_attention_max_rows(int kernel);
+
 int neb_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache,
                                const int32_t* block_table, int32_t block_table_rows,
                                int32_t max_blocks_per_seq, const int32_t* seq_lens,

@@ -27,6 +27,7 @@ SIGNATURES = {
     "neb_version": ([], ctypes.c_int),
     "neb_last_error": ([], ctypes.c_char_p),
     "neb_attention_workspace_bytes": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int], _sz),
+    "neb_attention_max_rows": ([ctypes.c_int], ctypes.c_int),
     "neb_paged_attention_decode": (_ATTN, ctypes.c_int),
     "neb_paged_attention_verify": (_ATTN, ctypes.c_int),
     "neb_paged_attention_decode_noalloc": (_ATTN[:18] + [_vp], ctypes.c_int),

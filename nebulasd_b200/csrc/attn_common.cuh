@@ -123,8 +123,79 @@ __device__ inline void merge_unit_warp(const AttnParams& p, int first_row, int n
   }
 }
 
+// The same merge spread over `nthreads` threads (tid in [0, nthreads)): a
+// thread owns (unit row, 4-column chunk) pairs, four at a time, and issues the
+// loads of all their slots (up to four slots per round) before using any, so
+// that a merge costs one or two memory round trips.  Slots fold in order with
+// a running maximum.
+static __device__ __noinline__ void merge_unit_threads(const AttnParams& p, int first_row, int nrows, int kv_head,
+                                                       int gqa, long long w0, long long w1, int tid, int nthreads) {
+  const int npairs = nrows * gqa * 32;
+  for (int base = tid; base < npairs; base += 4 * nthreads) {
+    float mx[4], den[4];
+    float4 acc[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      mx[q] = neg_inf();
+      den[q] = 0.f;
+      acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (long long wb = w0; wb <= w1; wb += 4) {
+      float le[4][4];
+      float4 v[4][4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int idx = base + q * nthreads;
+        const int j = idx >> 5, c = idx & 31;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          le[q][k] = neg_inf();
+          v[q][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (idx < npairs && wb + k <= w1) {
+            const long long slot = piece_slot(wb + k, w0);
+            le[q][k] = __ldcg(p.part_lse + slot * p.nq + j);
+            v[q][k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + (slot * p.nq + j) * kHeadDim) + c);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float cm = fmaxf(fmaxf(le[q][0], le[q][1]), fmaxf(le[q][2], le[q][3]));
+        if (cm == neg_inf()) continue;
+        if (cm > mx[q]) {
+          const float sc = fast_exp2(mx[q] - cm);  // 0 while nothing was folded in yet
+          acc[q].x *= sc; acc[q].y *= sc; acc[q].z *= sc; acc[q].w *= sc;
+          den[q] *= sc;
+          mx[q] = cm;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (le[q][k] == neg_inf()) continue;
+          const float wt = fast_exp2(le[q][k] - mx[q]);
+          acc[q].x += wt * v[q][k].x; acc[q].y += wt * v[q][k].y;
+          acc[q].z += wt * v[q][k].z; acc[q].w += wt * v[q][k].w;
+          den[q] += wt;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = base + q * nthreads;
+      if (idx >= npairs) continue;
+      const int j = idx >> 5, c = idx & 31;
+      const float inv = 1.f / den[q];
+      const int row = first_row + j / gqa;
+      const int head = kv_head * gqa + (j % gqa);
+      uint2 out;
+      out.x = f2_to_h2(acc[q].x * inv, acc[q].y * inv);
+      out.y = f2_to_h2(acc[q].z * inv, acc[q].w * inv);
+      *reinterpret_cast<uint2*>(p.o + ((long long)row * p.num_q_heads + head) * kHeadDim + c * 4) = out;
+    }
+  }
+}
+
 // Rows of groups with no tile (every length <= 0) get NaN, like the reference.
-__device__ inline void write_nan_rows(const AttnParams& p, const PlanSmem& ps, int ng, long long w,
+static __device__ __noinline__ void write_nan_rows(const AttnParams& p, const PlanSmem& ps, int ng, long long w,
                                       long long workers) {
   const int lane = threadIdx.x & 31;
   const uint2 nan2 = make_uint2(0x7e007e00u, 0x7e007e00u);

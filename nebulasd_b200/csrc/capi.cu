@@ -36,6 +36,7 @@ int launch_decode(const AttnParams& p, long long workers, cudaStream_t stream);
 long long verify_workers(int device);
 int verify_group_rows(int gqa);
 int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream);
+int verify_max_rows();
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
@@ -131,6 +132,11 @@ extern "C" {
 int neb_version(void) { return 100; }
 
 const char* neb_last_error(void) { return g_last_error; }
+
+int neb_attention_max_rows(int kernel) {
+  if (kernel == NEB_ATTN_VERIFY) return verify_max_rows();
+  return kernel == NEB_ATTN_DECODE ? kMaxRows : 0;
+}
 
 size_t neb_attention_workspace_bytes(int kernel, int device, int num_rows, int num_q_heads,
                                      int num_kv_heads) {

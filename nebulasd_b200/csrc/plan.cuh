@@ -70,7 +70,7 @@ __device__ __forceinline__ int block_inclusive_scan(int v, int* scratch) {
 
 // Builds the plan into `ps`.  `scratch` is 32 ints of shared memory.
 // Returns nothing; ps.misc[0] = number of groups.
-__device__ inline void build_plan(PlanSmem ps, int* scratch, const int32_t* __restrict__ seq_ids,
+static __device__ __noinline__ void build_plan(PlanSmem ps, int* scratch, const int32_t* __restrict__ seq_ids,
                                   const int32_t* __restrict__ seq_lens, int num_rows,
                                   int max_group_rows) {
   // Pass 1: group starts and first rows.

@@ -10,21 +10,41 @@
 // every KV tile is staged once into shared memory by TMA and consumed by the
 // tensor cores for all of them.
 //
-// One persistent CTA per SM (plan.cuh gives each an equal share of KV tiles)
-// with warp roles:
-//   warp 0      TMA producer: per 16-token KV block, two 64-column boxes of K
-//               and of V (128-byte swizzle) into a 4-stage ring (64 tokens/stage)
-//   warp 1      MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
-//               tile (M=128, N=64), then O += P V (V as an MN-major operand) into
-//               a TMEM accumulator (M=128, N=128)
+// One persistent CTA per SM (the driver places a single CTA that allocates
+// tensor memory on an SM); plan.cuh gives each an equal share of KV tiles.
+// The memory system runs saturated, so a global load on a critical path costs
+// microseconds: every role below waits only on its own inputs and every global
+// read it needs is issued well ahead.  K, S, softmax, P V and V of consecutive
+// 128-token stages overlap:
+//   warp 0      K producer: per 16-token KV block two 64-column TMA boxes
+//               (128-byte swizzle) into the K ring, once S of the stage that
+//               last used the slot is done; publishes the stage's block flags.
+//               Block-table rows are fetched two 32-tile batches ahead.
+//   warp 1      S issuer (one thread): Q of the next piece by TMA into the
+//               other half of a double buffer, S = Q K^T into a double-buffered
+//               TMEM tile (M=64, N=128).
 //   warps 2..5  softmax / epilogue: read S with tcgen05.ld, masked online
-//               softmax in the exp2 domain (lazy rescale of O: only when a row's
-//               max grows by more than 2^8), write P (fp16) to shared memory,
-//               normalise O at the end of a piece and store it, or store a
-//               partial and let the last-arriving CTA of the unit merge.
-// Query row j of a unit sits at MMA row 32*(j%4) + j/4, i.e. lanes 0..15 of
-// each TMEM lane quadrant, so all four softmax warps share the work and the
-// 16x256b TMEM loads give each thread two rows x 16 columns.
+//               softmax in the exp2 domain (O is rescaled only when a row's max
+//               grows by more than 2^8), P as fp16 in shared memory; at the end
+//               of a piece normalise O and store it, or store a partial.
+//   warp 6      V producer: the V boxes into the V ring, once P V of the
+//               stage that last used the slot is done.
+//   warp 7      P V issuer (one thread): O += P V (V an MN-major operand) into
+//               a TMEM accumulator (M=64, N=128) and the row sums of P as
+//               P x ones (N=16).
+// Once the pipeline has drained, the whole CTA finishes the pieces of units
+// split across CTAs (at most two per CTA, its first and its last): it counts
+// each partial in and, in the CTA that completes the unit, merges the
+// partials by log-sum-exp.
+//
+// Each role is an out-of-line function and the two producers share one, so
+// that the instruction cache holds every warp's hot loop at once: with more
+// code than that, the warps of an SM stall on instruction fetch.
+//
+// Query rows: a unit of nrows rows and gqa heads per row is cut into four
+// chunks of c = gqa*ceil(nrows/4) rows; chunk q goes to MMA rows 16q.. (TMEM
+// lane quadrant q, where an M=64 accumulator keeps rows 16q..16q+15), so one
+// 3D TMA box per chunk loads Q and each softmax warp owns one chunk.
 //
 // Every wait is bounded (about 2 s); on expiry the kernel records an error
 // bit, stops issuing work, waits (bounded) for its own copies and MMAs, frees
@@ -40,66 +60,67 @@
 namespace neb {
 using namespace sm100;
 
-// Timeline hooks: empty unless the library is built with -DNEB_TRACE, in which
-// case each CTA stamps %globaltimer into a caller-provided buffer (offline
-// profiling of the pipeline; the shipped build contains no tracing code).
-#ifdef NEB_TRACE
-__device__ unsigned long long* g_trace = nullptr;
-#define NEB_TRACE_POINT(i)                                                                      \
-  do {                                                                                          \
-    if (g_trace) {                                                                              \
-      unsigned long long t_;                                                                    \
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                    \
-      g_trace[blockIdx.x * 2048 + (i)] = t_;                                                     \
-    }                                                                                           \
-  } while (0)
-#else
-#define NEB_TRACE_POINT(i) \
-  do {                     \
-  } while (0)
-#endif
-
-constexpr int kVThreads = 384;        // 12 warps: 0 TMA, 1 MMA, 2-3 idle, 4-11 softmax
-constexpr int kSoftmaxWarp0 = 4;
-constexpr int kSoftmaxThreads = 256;
-constexpr int kStageBlocks = 4;    // 16-token KV blocks per pipeline stage
-constexpr int kStages = 4;         // KV ring depth
-constexpr int kMaxQRows = 128;     // query rows per unit: the MMA's M
-constexpr uint32_t kTmemCols = 512;  // S: 2 x 64 columns, O: 128 columns, row sums: 16 columns
-constexpr uint32_t kOCol = 128;
-constexpr uint32_t kSumCol = 256;   // P x ones: every column holds the row's running sum of P
-
+constexpr int kVThreads = 256;  // 8 warps: 0 K, 1 S, 2-5 softmax, 6 V, 7 P V
+constexpr int kKWarp = 0;
+constexpr int kSWarp = 1;
+constexpr int kSoftmaxWarp0 = 2;
+constexpr int kSoftmaxThreads = 128;
+constexpr int kVWarp = 6;
+constexpr int kPVWarp = 7;
+constexpr int kStageBlocks = 4;                           // 16-token KV blocks per stage
+constexpr int kStageCols = kStageBlocks * kBlockTokens;   // tokens per stage: the S tile's N
+constexpr int kStageR = kStageCols / 8;                   // 8-column groups of an S tile
+constexpr int kRing = 4;                                  // depth of the K ring and of the V ring
+constexpr int kSBufs = 4;                                 // S tiles in TMEM (the S issuer runs ahead)
+constexpr int kFlagSlots = kRing + kSBufs;                // block-flag ring (see the K producer)
+constexpr int kMaxQRows = 64;                             // query rows per unit: the MMA's M
+constexpr int kMaxGqa = 16;                               // a row's heads fit one 16-row chunk
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSBuf = 64;                            // S tile b at columns 64*b
+constexpr uint32_t kOCol = 256;                           // O: 128 columns
+constexpr uint32_t kSumCol = 384;                         // P x ones: every column holds the row sum
 constexpr long long kWaitLimit = 4000000000LL;
+static_assert(kStageCols <= (int)kSBuf && kStageR % 2 == 0 && kSBufs * kSBuf <= kOCol, "S tiles fit TMEM");
 
 // Shared memory map (offsets from a 1024-byte aligned base).
-constexpr uint32_t kQOff = 0;                               // 2 d-halves x 128 rows x 128 B
-constexpr uint32_t kKVOff = 32768;                          // per stage: K (2 x 8 KiB), V (2 x 8 KiB)
-constexpr uint32_t kStageBytes = 32768;
-constexpr uint32_t kPOff = kKVOff + kStages * kStageBytes;  // 2 buffers x 128 rows x 128 B
-constexpr uint32_t kOnesOff = kPOff + 2 * 16384;            // 16 rows x 128 B of fp16 ones (row-sum MMA)
+constexpr uint32_t kQHalf = kMaxQRows * 128;       // one 64-column half of Q
+constexpr uint32_t kQBuf = 2 * kQHalf;             // Q of one piece
+constexpr uint32_t kQOff = 0;                      // two Q buffers
+constexpr uint32_t kHalf = kStageBlocks * 2048;    // one 64-column half of K or V of a stage
+constexpr uint32_t kSlotBytes = 2 * kHalf;         // a ring slot: both halves of K (or V)
+constexpr uint32_t kKOff = kQOff + 2 * kQBuf;
+constexpr uint32_t kVOff = kKOff + kRing * kSlotBytes;
+constexpr uint32_t kPAtom = kMaxQRows * 128;       // 64 rows x 64 fp16 of P (one swizzle column)
+constexpr uint32_t kPBuf = ((kStageCols + 63) / 64) * kPAtom;
+constexpr uint32_t kPOff = kVOff + kRing * kSlotBytes;
+constexpr uint32_t kOnesOff = kPOff + 2 * kPBuf;   // 16 rows x 128 B of fp16 ones
 constexpr uint32_t kBarOff = kOnesOff + 2048;
 constexpr uint32_t kPlanOff = kBarOff + 1024;
-constexpr int kVerifyMaxRows = 3900;  // keeps the plan arrays inside 227 KiB of shared memory
+static_assert(kHalf % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+
+// Largest row count whose plan arrays still fit next to the fixed buffers
+// (227 KiB per CTA, less the alignment pad and 256 bytes of static shared memory).
+constexpr int kVerifyMaxRows = ((232448 - 1024 - 256 - (int)kPlanOff) / 4 - 8) / 2 - 1;
+static_assert(kVerifyMaxRows >= 1024, "room for the plan of a large verify batch");
 
 struct VerifyShared {
-  uint64_t kv_full[kStages];   // K and V of a stage landed (softmax reads the block flags)
-  uint64_t k_full[kStages];    // K landed
-  uint64_t v_full[kStages];    // V landed
-  uint64_t k_empty[kStages];   // S of the stage completed: K slot reusable
-  uint64_t kv_empty[kStages];  // O += P V of the stage completed: V slot reusable
-  uint64_t s_full[2];
-  uint64_t s_empty[2];
+  uint64_t k_full[kRing];        // K landed
+  uint64_t k_empty[kRing];       // S of the slot's stage completed
+  uint64_t v_full[kRing];        // V landed
+  uint64_t v_empty[kRing];       // P V of the slot's stage completed
+  uint64_t flags_full[kFlagSlots];
+  uint64_t s_full[kSBufs];
+  uint64_t s_empty[kSBufs];
   uint64_t p_full[2];
   uint64_t pv_done[2];
-  uint64_t q_full;
-  uint64_t q_empty;
+  uint64_t q_full[2];
+  uint64_t q_empty[2];
   uint64_t o_empty;
-  uint64_t mma_final;
-  uint64_t epi_bar;  // bounded barrier of the 128 softmax threads
+  uint64_t s_final;
+  uint64_t pv_final;
   uint32_t tmem_base;
   int32_t abort_flag;
-  int32_t last_flag;
-  int32_t blk[kStages][kStageBlocks];
+  int32_t blk[kFlagSlots][kStageBlocks];
 };
 static_assert(sizeof(VerifyShared) <= 1024, "barrier block fits its slot");
 
@@ -112,12 +133,66 @@ struct VerifyArgs {
   int oob_row;  // first row past the end of the K/V tensor maps (loads there return zeros)
 };
 
+// What every role needs to know about the launch and its own CTA.
+struct Ctx {
+  const AttnParams* p;
+  VerifyShared* sh;
+  uint8_t* smem;
+  PlanSmem ps;
+  int ng, hk, gqa, oob_row;
+  long long total, workers, w, t_begin, t_end;
+  uint32_t tmem;
+  unsigned long long* trace;  // timeline buffer row of this CTA (builds with NEB_TRACE only)
+};
+
+// Timeline hooks: empty unless the library is built with -DNEB_TRACE, in which
+// case each CTA stamps %globaltimer into a caller-provided buffer (offline
+// profiling of the pipeline; the shipped build contains no tracing code).
+#ifdef NEB_TRACE
+__device__ unsigned long long* g_trace = nullptr;
+#define NEB_TRACE_POINT(c, i)                                \
+  do {                                                       \
+    if ((c).trace) {                                         \
+      unsigned long long t_;                                 \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); \
+      (c).trace[(i)] = t_;                                   \
+    }                                                        \
+  } while (0)
+#define NEB_PHASE_DECL() long long neb_ph[4] = {0, 0, 0, 0}, neb_t = clock64()
+#define NEB_PHASE(k)                 \
+  do {                               \
+    const long long t2_ = clock64(); \
+    neb_ph[(k)] += t2_ - neb_t;      \
+    neb_t = t2_;                     \
+  } while (0)
+#define NEB_PHASE_DUMP(c, n)                                                   \
+  do {                                                                         \
+    if ((c).trace && threadIdx.x == kSoftmaxWarp0 * 32) {                      \
+      for (int k_ = 0; k_ < 4; ++k_) (c).trace[2000 + k_] = neb_ph[k_];        \
+      (c).trace[2004] = (n);                                                   \
+    }                                                                          \
+  } while (0)
+#else
+#define NEB_TRACE_POINT(c, i) \
+  do {                        \
+  } while (0)
+#define NEB_PHASE_DECL() \
+  do {                   \
+  } while (0)
+#define NEB_PHASE(k) \
+  do {               \
+  } while (0)
+#define NEB_PHASE_DUMP(c, n) \
+  do {                       \
+  } while (0)
+#endif
+
 // The pieces of one worker: a cursor over its tile range (plan.cuh).
 struct PieceCursor {
   const PlanSmem* ps;
   int ng, hk, g;
   long long t, t_end;
-  __device__ void init(const PlanSmem* planp, int ngroups, int kvh, long long begin, long long end) {
+  __device__ __noinline__ void init(const PlanSmem* planp, int ngroups, int kvh, long long begin, long long end) {
     ps = planp;
     ng = ngroups;
     hk = kvh;
@@ -125,14 +200,15 @@ struct PieceCursor {
     t_end = end;
     g = begin < end ? find_group(ps->gprefix, ng, begin, hk) : 0;
   }
-  // Fills (g, kv_head, tile_lo, tile_hi, nb, unit_start); false when done.
-  __device__ bool next(int& grp, int& kv_head, int& lo, int& hi, int& nb, long long& unit_start) {
+  // Fills (group, kv_head, tile_lo, tile_hi, nb, unit_start); false when done.
+  __device__ __forceinline__ bool next(int& grp, int& kv_head, int& lo, int& hi, int& nb, long long& unit_start) {
     if (t >= t_end) return false;
     while ((long long)hk * ps->gprefix[g + 1] <= t) ++g;
     nb = ps->gprefix[g + 1] - ps->gprefix[g];
     const long long gbase = (long long)hk * ps->gprefix[g];
-    kv_head = (int)((t - gbase) / nb);
-    lo = (int)(t - gbase - (long long)kv_head * nb);
+    const int rel = (int)(t - gbase);  // < hk * nb
+    kv_head = rel / nb;
+    lo = rel - kv_head * nb;
     const int cnt = (int)min((long long)(nb - lo), t_end - t);
     hi = lo + cnt;
     unit_start = gbase + (long long)kv_head * nb;
@@ -144,17 +220,21 @@ struct PieceCursor {
 
 __device__ __forceinline__ int stages_of(int lo, int hi) { return (hi - lo + kStageBlocks - 1) / kStageBlocks; }
 
+// Query rows per TMEM lane quadrant for a group of `nrows` rows.
+__device__ __forceinline__ int rows_per_quad(int nrows) { return (nrows + 3) >> 2; }
+
 __device__ __forceinline__ void raise_abort(VerifyShared* sh, const AttnParams& p) {
   if (atomicExch(&sh->abort_flag, 1) == 0) record_error(p, kErrTimeout);
 }
 __device__ __forceinline__ bool aborted(VerifyShared* sh) {
   return *reinterpret_cast<volatile int32_t*>(&sh->abort_flag) != 0;
 }
-__device__ __forceinline__ bool wait_or_abort(VerifyShared* sh, const AttnParams& p, uint64_t* bar,
-                                              uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Slow path of wait_or_abort, out of line: one copy serves every call site.
+// The thread sleeps in hardware while the phase is incomplete.
+__device__ __noinline__ bool wait_or_abort_slow(VerifyShared* sh, const AttnParams& p, uint64_t* bar,
+                                                uint32_t parity) {
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, 20000)) {
     if (aborted(sh) || clock64() - t0 > kWaitLimit) {
       raise_abort(sh, p);
       return false;
@@ -162,27 +242,653 @@ __device__ __forceinline__ bool wait_or_abort(VerifyShared* sh, const AttnParams
   }
   return true;
 }
+__device__ __forceinline__ bool wait_or_abort(VerifyShared* sh, const AttnParams& p, uint64_t* bar,
+                                              uint32_t parity) {
+  return mbar_try_wait(bar, parity) || wait_or_abort_slow(sh, p, bar, parity);
+}
 
 // One arrival per softmax warp (count 4): the warp's lanes are first gathered
-// with __syncwarp, which orders their earlier shared/tensor-memory work.
+// with __syncwarp, which orders their earlier shared/tensor/global memory work.
 __device__ __forceinline__ void warp_arrive(uint64_t* bar) {
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
-// Barrier of the 128 softmax threads built on an mbarrier, so that it is bounded.
-__device__ __forceinline__ bool epi_sync(VerifyShared* sh, const AttnParams& p, uint32_t& phase) {
-  warp_arrive(&sh->epi_bar);
-  const bool ok = wait_or_abort(sh, p, &sh->epi_bar, phase & 1);
-  ++phase;
-  return ok;
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) { return f2_to_h2(a, b); }
+
+__device__ __forceinline__ void scale_rows(uint32_t* r, int n4, float alpha_a, float alpha_b) {
+#pragma unroll
+  for (int i = 0; i < n4; ++i) {
+    r[4 * i + 0] = __float_as_uint(__uint_as_float(r[4 * i + 0]) * alpha_a);
+    r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) * alpha_a);
+    r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) * alpha_b);
+    r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) * alpha_b);
+  }
 }
 
-__device__ __forceinline__ uint32_t pack_half2(float a, float b) { return f2_to_h2(a, b); }
+// Exchanges the two query rows a thread holds in a 16x256b TMEM load
+// (row a in registers 4r, 4r+1; row b in 4r+2, 4r+3).
+template <int N>
+__device__ __forceinline__ void swap_rows_n(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const uint32_t t0 = r[4 * i], t1 = r[4 * i + 1];
+    r[4 * i] = r[4 * i + 2];
+    r[4 * i + 1] = r[4 * i + 3];
+    r[4 * i + 2] = t0;
+    r[4 * i + 3] = t1;
+  }
+}
+
+// Block-table rows of a producer warp's tiles, in the order the warp consumes
+// them (the worker's flattened tile range).  Lane l holds tile base + 32k + l
+// of batch k = 0, 1, 2; batch 2 is in flight while batches 0 and 1 are used.
+struct TileFeed {
+  const AttnParams* p;
+  const PlanSmem* ps;
+  int ng, oob_row;
+  long long t_end, base;
+  int r0, v0, r1, v1, r2, v2;
+
+  // The fetch of one lane's tile in two steps, so that several batches' loads
+  // can be in flight together: locate() finds the unit and reads the seq id,
+  // resolve() reads the block-table entry.
+  struct Pending {
+    int sid, tile, kv_head;
+    bool in_range;  // false: tile past the worker's range
+  };
+  __device__ __forceinline__ Pending locate(long long bt) const {
+    Pending q{0, 0, 0, false};
+    const long long t = bt + (threadIdx.x & 31);
+    if (t >= t_end) return q;
+    const int hk = p->num_kv_heads;
+    const int g = find_group(ps->gprefix, ng, t, hk);
+    const int nb = ps->gprefix[g + 1] - ps->gprefix[g];
+    const int rel = (int)(t - (long long)hk * ps->gprefix[g]);  // < hk * nb
+    q.kv_head = rel / nb;
+    q.tile = rel - q.kv_head * nb;
+    q.sid = __ldg(p->seq_ids + ps->gfirst[g]);
+    q.in_range = true;
+    return q;
+  }
+  __device__ __forceinline__ void resolve(const Pending& q, int& r, int& v) const {
+    r = oob_row;
+    v = 0;
+    if (!q.in_range) return;
+    const long long blk = lookup_block(*p, q.sid, q.tile);
+    if (blk >= 0) {
+      v = 1;
+      r = (int)(((blk * p->num_layers + p->cur_layer) * p->num_kv_heads + q.kv_head) * kBlockTokens);
+    }
+  }
+  __device__ __forceinline__ void fetch(long long bt, int& r, int& v) const { resolve(locate(bt), r, v); }
+  __device__ void init(const AttnParams* pp, const PlanSmem* pps, int ngroups, int oob, long long begin,
+                       long long end) {
+    p = pp;
+    ps = pps;
+    ng = ngroups;
+    oob_row = oob;
+    t_end = end;
+    base = begin;
+    const Pending q0 = locate(base), q1 = locate(base + 32), q2 = locate(base + 64);
+    resolve(q0, r0, v0);
+    resolve(q1, r1, v1);
+    resolve(q2, r2, v2);
+  }
+  // Row and flag of tile pos + b (warp-uniform arguments, base <= pos + b < base + 64).
+  __device__ __forceinline__ void get(long long pos, int b, int& r, int& v) const {
+    const int d = (int)(pos + b - base);
+    const int rr = d < 32 ? r0 : r1, vv = d < 32 ? v0 : v1;
+    r = __shfl_sync(0xffffffffu, rr, d & 31);
+    v = __shfl_sync(0xffffffffu, vv, d & 31);
+  }
+  // Drops the batches before `pos` and starts fetching the ones after.
+  __device__ __forceinline__ void advance(long long pos) {
+    while (pos >= base + 32) {
+      r0 = r1; v0 = v1;
+      r1 = r2; v1 = v2;
+      base += 32;
+      fetch(base + 64, r2, v2);
+    }
+  }
+};
+
+// ------------------------------------------------------------------ producers
+// One function serves the K warp (flags != 0: it also publishes the block
+// flags) and the V warp.  Slot G % kRing frees when the MMA that read it (S for
+// K, P V for V) of stage G - kRing is done.  The block flags of stage G go to
+// flag slot G % kFlagSlots: its previous reader, the softmax of stage
+// G - kFlagSlots, reads the flags before it releases S of that stage, which
+// S(G - kRing) (issued only once S buffer (G - kRing) % kSBufs was released by
+// the softmax of stage G - kRing - kSBufs), and so this load, had to wait for.
+__device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uint64_t* full, uint64_t* empty,
+                                      uint32_t ring_off, int flags) {
+  const AttnParams& p = *c.p;
+  VerifyShared* sh = c.sh;
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) tma_prefetch_desc(tmap);
+  TileFeed feed;
+  feed.init(&p, &c.ps, c.ng, c.oob_row, c.t_begin, c.t_end);
+  PieceCursor cur;
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  int g, h, lo, hi, nb;
+  long long ustart;
+  int G = 0;
+  long long pos = c.t_begin;
+  bool ok = true;
+  while (ok && cur.next(g, h, lo, hi, nb, ustart)) {
+    const int nst = stages_of(lo, hi);
+    for (int s = 0; s < nst; ++s, ++G) {
+      const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
+      int rows[kStageBlocks], valid[kStageBlocks];
+#pragma unroll
+      for (int b = 0; b < kStageBlocks; ++b) feed.get(pos, b, rows[b], valid[b]);
+      int waited = 1;
+      if (lane == 0) {
+        const int slot = G % kRing;
+        waited = wait_or_abort(sh, p, &empty[slot], (uint32_t)(((G / kRing) & 1) ^ 1));
+        if (waited) {
+          if (G < 100) NEB_TRACE_POINT(c, (flags ? 8 : 508) + G);
+          if (flags) {
+            const int fs = G % kFlagSlots;
+#pragma unroll
+            for (int b = 0; b < kStageBlocks; ++b) sh->blk[fs][b] = b < nblk ? valid[b] : 0;
+            mbar_arrive(&sh->flags_full[fs]);
+          }
+          uint8_t* dst = c.smem + ring_off + slot * kSlotBytes;
+          mbar_arrive_expect_tx(&full[slot], (uint32_t)nblk * 2u * 2048u);
+#pragma unroll 1
+          for (int b = 0; b < nblk; ++b) {
+            tma_load_2d(dst + b * 2048, tmap, &full[slot], 0, rows[b]);
+            tma_load_2d(dst + kHalf + b * 2048, tmap, &full[slot], 64, rows[b]);
+          }
+        }
+      }
+      waited = __shfl_sync(0xffffffffu, waited, 0);
+      if (!waited) {
+        ok = false;
+        break;
+      }
+      pos += nblk;
+      feed.advance(pos);
+    }
+  }
+  // Wait (bounded) for every copy this warp issued before the CTA can exit.
+  if (lane == 0)
+#pragma unroll 1
+    for (int Gi = (G > kRing ? G - kRing : 0); Gi < G; ++Gi)
+      mbar_wait(&full[Gi % kRing], (uint32_t)((Gi / kRing) & 1), kWaitLimit);
+}
+
+// After the pipeline has drained, the whole CTA counts its split pieces in
+// (at most two: its first and its last piece) and merges the units it
+// completes.  Every thread has passed a CTA barrier after the softmax warps'
+// partial stores, so one fence per thread publishes them, with the counts, to
+// the other CTAs.
+__device__ __noinline__ void finish_split_units(const Ctx& c, int* flags) {
+  const AttnParams& p = *c.p;
+  PieceCursor cur;
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  int g[2], h[2], lo, hi, nb;
+  long long us[2], ustart;
+  int k = 0;
+  while (k < 2 && cur.next(g[k], h[k], lo, hi, nb, ustart)) {
+    if (lo == 0 && hi == nb) continue;
+    us[k++] = ustart;
+  }
+  if (k == 0) return;
+  if (threadIdx.x < k) {
+    // The CTA barrier before this call ordered every thread's partial stores
+    // before this fence, which publishes them with the count.
+    __threadfence();
+    const int i = threadIdx.x;
+    const int nbi = c.ps.gprefix[g[i] + 1] - c.ps.gprefix[g[i]];
+    const long long w0 = worker_of(us[i], c.total, c.workers);
+    const long long w1 = worker_of(us[i] + nbi - 1, c.total, c.workers);
+    const long long unit = (long long)g[i] * c.hk + h[i];
+    const int last = atomicAdd(p.counters + unit, 1) == (int)(w1 - w0);
+    if (last) p.counters[unit] = 0;  // every piece has arrived: ready for the next call
+    flags[i] = last;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 1700);
+#pragma unroll 1
+  for (int i = 0; i < k; ++i) {
+    if (!flags[i]) continue;
+    __threadfence();
+    const int nbi = c.ps.gprefix[g[i] + 1] - c.ps.gprefix[g[i]];
+    const long long w0 = worker_of(us[i], c.total, c.workers);
+    const long long w1 = worker_of(us[i] + nbi - 1, c.total, c.workers);
+    const int first_row = c.ps.gfirst[g[i]];
+    merge_unit_threads(p, first_row, c.ps.gfirst[g[i] + 1] - first_row, h[i], c.gqa, w0, w1, threadIdx.x,
+                       kVThreads);
+    if (threadIdx.x == 0) NEB_TRACE_POINT(c, 1701 + i);
+  }
+}
+
+// ------------------------------------------------------------------- S issuer
+// Q of piece i goes to buffer i % 2 as soon as piece i - 2 is done with it,
+// i.e. a whole piece ahead of its first S.
+struct QFeeder {
+  PieceCursor cur;
+  int qi, qg, qh, qlo, qhi, qnb;
+  long long qus;
+  bool qhave;
+  // Issues the Q loads that may go now; blocks only for piece `need`.
+  __device__ __noinline__ bool feed(const Ctx& c, const CUtensorMap* tmap_q, int cur_piece, int need) {
+    VerifyShared* sh = c.sh;
+    while (qhave && qi <= cur_piece + 1) {
+      const int b = qi & 1;
+      if (qi >= 2) {
+        const uint32_t par = (uint32_t)(((qi - 2) >> 1) & 1);
+        if (qi > need) {
+          if (!mbar_test_wait(&sh->q_empty[b], par)) return true;
+        } else if (!wait_or_abort(sh, *c.p, &sh->q_empty[b], par)) {
+          return false;
+        }
+      }
+      const int first_row = c.ps.gfirst[qg];
+      const int nrows = c.ps.gfirst[qg + 1] - first_row;
+      const int rq = rows_per_quad(nrows);
+      const int nquads = (nrows + rq - 1) / rq;
+      mbar_arrive_expect_tx(&sh->q_full[b], (uint32_t)nquads * 2u * 2048u);
+#pragma unroll 1
+      for (int q = 0; q < nquads; ++q)
+        for (int dh = 0; dh < 2; ++dh)
+          tma_load_3d(c.smem + kQOff + b * kQBuf + dh * kQHalf + q * 16 * 128, tmap_q, &sh->q_full[b], dh * 64,
+                      qh * c.gqa, first_row + q * rq);
+      ++qi;
+      qhave = cur.next(qg, qh, qlo, qhi, qnb, qus);
+    }
+    return true;
+  }
+};
+
+__device__ __noinline__ void s_issuer(const Ctx& c, const CUtensorMap* tmap_q) {
+  const AttnParams& p = *c.p;
+  VerifyShared* sh = c.sh;
+  tma_prefetch_desc(tmap_q);
+  const uint32_t q_base = smem_u32(c.smem + kQOff);
+  const uint32_t k_base = smem_u32(c.smem + kKOff);
+  const uint32_t tmem = c.tmem;
+  QFeeder qf;
+  qf.cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  qf.qi = 0;
+  qf.qhave = qf.cur.next(qf.qg, qf.qh, qf.qlo, qf.qhi, qf.qnb, qf.qus);
+  PieceCursor cur;
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  int g, h, lo, hi, nb;
+  long long ustart;
+  int G = 0;
+  bool ok = true;
+  for (int piece = 0; ok && cur.next(g, h, lo, hi, nb, ustart); ++piece) {
+    const int nst = stages_of(lo, hi);
+    const int b = piece & 1;
+    if (!qf.feed(c, tmap_q, piece, piece) || !wait_or_abort(sh, p, &sh->q_full[b], (uint32_t)((piece >> 1) & 1)))
+      break;
+    const uint32_t qb = q_base + b * kQBuf;
+    for (int s = 0; s < nst; ++s, ++G) {
+      const int slot = G % kRing, sb = G % kSBufs;
+      if (!wait_or_abort(sh, p, &sh->k_full[slot], (uint32_t)((G / kRing) & 1)) ||
+          !wait_or_abort(sh, p, &sh->s_empty[sb], (uint32_t)(((G / kSBufs) & 1) ^ 1))) {
+        ok = false;
+        break;
+      }
+      if (G < 100) NEB_TRACE_POINT(c, 108 + G);
+      tc_fence_after();
+      const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
+      const uint32_t idesc_s = idesc_f16_f32(kMaxQRows, 16 * nblk, false, false);
+      const uint32_t kst = k_base + slot * kSlotBytes;
+#pragma unroll 1
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t a = smem_desc_sw128(qb + (kk >> 2) * kQHalf + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = smem_desc_sw128(kst + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+        mma_f16(tmem + sb * kSBuf, a, bd, idesc_s, kk > 0 ? 1u : 0u);
+      }
+      mma_commit(&sh->s_full[sb]);
+      mma_commit(&sh->k_empty[slot]);
+      if (s == nst - 1) mma_commit(&sh->q_empty[b]);
+      if (qf.qhave && qf.qi <= piece + 1 && !qf.feed(c, tmap_q, piece, piece)) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  mma_commit(&sh->s_final);
+  mbar_wait(&sh->s_final, 0, kWaitLimit);
+  // Q loads issued for pieces that never ran (after an abort) must land before exit.
+#pragma unroll 1
+  for (int i = (qf.qi > 2 ? qf.qi - 2 : 0); i < qf.qi; ++i)
+    mbar_wait(&sh->q_full[i & 1], (uint32_t)((i >> 1) & 1), kWaitLimit);
+}
+
+// ----------------------------------------------------------------- P V issuer
+__device__ __noinline__ void pv_issuer(const Ctx& c) {
+  const AttnParams& p = *c.p;
+  VerifyShared* sh = c.sh;
+  const uint32_t v_base = smem_u32(c.smem + kVOff);
+  const uint32_t p_base = smem_u32(c.smem + kPOff);
+  const uint32_t ones_base = smem_u32(c.smem + kOnesOff);
+  const uint32_t idesc_pv = idesc_f16_f32(kMaxQRows, 128, false, true);
+  const uint32_t idesc_sum = idesc_f16_f32(kMaxQRows, 16, false, false);
+  const uint32_t tmem = c.tmem;
+  PieceCursor cur;
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  int g, h, lo, hi, nb;
+  long long ustart;
+  int G = 0;
+  bool ok = true;
+  for (int piece = 0; ok && cur.next(g, h, lo, hi, nb, ustart); ++piece) {
+    const int nst = stages_of(lo, hi);
+    for (int s = 0; s < nst; ++s, ++G) {
+      const int slot = G % kRing, sb = G & 1;
+      if (!wait_or_abort(sh, p, &sh->p_full[sb], (uint32_t)((G >> 1) & 1)) ||
+          !wait_or_abort(sh, p, &sh->v_full[slot], (uint32_t)((G / kRing) & 1)) ||
+          (s == 0 && piece > 0 && !wait_or_abort(sh, p, &sh->o_empty, (uint32_t)((piece - 1) & 1)))) {
+        ok = false;
+        break;
+      }
+      if (G < 100) NEB_TRACE_POINT(c, 208 + G);
+      tc_fence_after();
+      const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
+      const uint32_t vst = v_base + slot * kSlotBytes;
+#pragma unroll 1
+      for (int kb = 0; kb < nblk; ++kb) {
+        const uint64_t a = smem_desc_sw128(p_base + sb * kPBuf + (kb >> 2) * kPAtom + (kb & 3) * 32, 16, 1024);
+        const uint64_t b = smem_desc_sw128(vst + kb * 2048, kHalf, 1024);
+        const uint32_t acc = (s == 0 && kb == 0) ? 0u : 1u;
+        mma_f16(tmem + kOCol, a, b, idesc_pv, acc);
+        mma_f16(tmem + kSumCol, a, smem_desc_sw128(ones_base + (kb & 3) * 32, 16, 1024), idesc_sum, acc);
+      }
+      mma_commit(&sh->v_empty[slot]);
+      mma_commit(&sh->pv_done[sb]);
+    }
+  }
+  mma_commit(&sh->pv_final);
+  mbar_wait(&sh->pv_final, 0, kWaitLimit);
+}
+
+// -------------------------------------------------------------------- softmax
+// O and the row sums times (alpha_a, alpha_b), in TMEM (rare: a row's max grew
+// by more than 2^8).
+__device__ __noinline__ void rescale_o(uint32_t tmem, uint32_t lane_addr, float alpha_a, float alpha_b) {
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    uint32_t orr[32];
+    const uint32_t oaddr = tmem + kOCol + half * 64 + lane_addr;
+    tmem_ld_16x256b_x8(oaddr, orr);
+    tmem_wait_ld();
+    scale_rows(orr, 8, alpha_a, alpha_b);
+    tmem_st_16x256b_x8(oaddr, orr);
+  }
+  uint32_t srr[8];
+  tmem_ld_16x256b_x2(tmem + kSumCol + lane_addr, srr);
+  tmem_wait_ld();
+  scale_rows(srr, 2, alpha_a, alpha_b);
+  tmem_st_16x256b_x2(tmem + kSumCol + lane_addr, srr);
+  tmem_wait_st();
+}
+
+// The rows this thread owns in the current piece and their running state.
+struct SoftmaxRows {
+  int g, h, lo, hi, nb;
+  long long ustart;
+  int ja, jb, len_a, len_b;  // unit rows (-1: none) and their lengths
+};
+
+// End of a piece: O / l as fp16 output rows, or a partial (O / l, and
+// m + log2 l) for the merge; the PV issuer may reuse O once it is read.
+__device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, int G_last, float m_a, float m_b) {
+  const AttnParams& p = *c.p;
+  VerifyShared* sh = c.sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q4 = lane & 3;
+  const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
+  const int gqa = c.gqa;
+  if (!wait_or_abort(sh, p, &sh->pv_done[G_last & 1], (uint32_t)((G_last >> 1) & 1))) return false;
+  if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1508 + G_last);
+  tc_fence_after();
+  uint32_t sums[8];
+  tmem_ld_16x256b_x2(c.tmem + kSumCol + lane_addr, sums);
+  tmem_wait_ld();
+  const float l_a = __uint_as_float(sums[0]), l_b = __uint_as_float(sums[2]);
+  if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1900 + G_last);
+  const bool whole = (r.lo == 0 && r.hi == r.nb);
+  const long long slot = whole ? 0 : piece_slot(c.w, worker_of(r.ustart, c.total, c.workers));
+  const int first_row = c.ps.gfirst[r.g];
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    uint32_t o[32];
+    tmem_ld_16x256b_x8(c.tmem + kOCol + half * 64 + lane_addr, o);
+    tmem_wait_ld();
+    if (half == 1) {
+      tc_fence_before();
+      warp_arrive(&sh->o_empty);
+    }
+#pragma unroll 1
+    for (int x = 0; x < 2; ++x) {
+      const int j = x == 0 ? r.ja : r.jb;
+      if (j >= 0) {
+        const float inv = 1.f / (x == 0 ? l_a : l_b);
+        const int row = first_row + j / gqa;
+        const int head = r.h * gqa + j % gqa;
+        if (whole) {
+          __half* dst = p.o + ((long long)row * p.num_q_heads + head) * kHeadDim + half * 64;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint32_t*>(dst + 8 * i + 2 * q4) =
+                pack_half2(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv);
+        } else {
+          float* dst = p.part_o + (slot * p.nq + j) * kHeadDim + half * 64;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            __stcg(reinterpret_cast<float2*>(dst + 8 * i + 2 * q4),
+                   make_float2(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv));
+          if (half == 0 && q4 == 0) {
+            const float l = x == 0 ? l_a : l_b;
+            const float m = x == 0 ? m_a : m_b;
+            __stcg(p.part_lse + slot * p.nq + j, l > 0.f ? m + __log2f(l) : neg_inf());
+          }
+        }
+      }
+      swap_rows_n<8>(o);  // row b's values into row a's registers
+    }
+  }
+  if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1800 + G_last);
+  return true;
+}
+
+__device__ __noinline__ void softmax_role(const Ctx& c) {
+  const AttnParams& p = *c.p;
+  VerifyShared* sh = c.sh;
+  uint8_t* smem = c.smem;
+  const uint32_t tmem = c.tmem;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x - kSoftmaxWarp0 * 32;  // 0..127
+  const int qd = warp & 3;                             // TMEM lane quadrant of this warp
+  const int q4 = lane & 3;
+  const int li_a = lane >> 2, li_b = li_a + 8;          // lanes within the quadrant
+  const int ma = 16 * qd + li_a, mb = ma + 8;           // MMA rows
+  const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
+  const float sc = p.scale_log2;
+  const int gqa = c.gqa;
+  // Clear P once (rows no unit writes must hold finite values) and write the
+  // ones tile of the row-sum MMA; the barrier orders the clearing before
+  // any thread's first P store.
+#pragma unroll 1
+  for (int i = tid; i < (int)(2 * kPBuf) / 16; i += kSoftmaxThreads)
+    *reinterpret_cast<uint4*>(smem + kPOff + i * 16) = make_uint4(0, 0, 0, 0);
+#pragma unroll 1
+  for (int i = tid; i < 2048 / 16; i += kSoftmaxThreads)
+    *reinterpret_cast<uint4*>(smem + kOnesOff + i * 16) = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+  fence_proxy_async_smem();
+  named_bar_sync(1, kSoftmaxThreads);
+  PieceCursor cur;
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  // Unit rows of this thread in a piece's group, and their lengths (loaded a
+  // piece ahead of use).
+  auto fill = [&](SoftmaxRows& r) -> bool {
+    if (!cur.next(r.g, r.h, r.lo, r.hi, r.nb, r.ustart)) return false;
+    const int first_row = c.ps.gfirst[r.g];
+    const int nrows = c.ps.gfirst[r.g + 1] - first_row;
+    const int cq = gqa * rows_per_quad(nrows), nq = nrows * gqa;
+    r.ja = (li_a < cq && qd * cq + li_a < nq) ? qd * cq + li_a : -1;
+    r.jb = (li_b < cq && qd * cq + li_b < nq) ? qd * cq + li_b : -1;
+    r.len_a = r.ja >= 0 ? __ldg(p.seq_lens + first_row + r.ja / gqa) : -1;
+    r.len_b = r.jb >= 0 ? __ldg(p.seq_lens + first_row + r.jb / gqa) : -1;
+    return true;
+  };
+  SoftmaxRows cr, nr;
+  bool have = fill(cr);
+  int G = 0;
+  bool ok = true;
+  NEB_PHASE_DECL();
+  while (have && ok) {
+    const bool have_next = fill(nr);
+    if (tid == 0 && G < 100) NEB_TRACE_POINT(c, 1400 + G);
+    const bool has_b = __any_sync(0xffffffffu, cr.jb >= 0);  // warp-uniform
+    float m_a = neg_inf(), m_b = neg_inf();
+    const int nst = stages_of(cr.lo, cr.hi);
+    for (int s = 0; s < nst; ++s, ++G) {
+      const int fs = G % kFlagSlots;
+      const int sbuf = G % kSBufs;  // S tile in TMEM
+      const int sb = G & 1;         // P buffer
+      if (!wait_or_abort(sh, p, &sh->flags_full[fs], (uint32_t)((G / kFlagSlots) & 1)) ||
+          !wait_or_abort(sh, p, &sh->s_full[sbuf], (uint32_t)((G / kSBufs) & 1))) {
+        ok = false;
+        break;
+      }
+      if (tid == 0 && G < 100) NEB_TRACE_POINT(c, 308 + G);
+      NEB_PHASE(0);
+      tc_fence_after();
+      uint32_t sr[4 * kStageR];
+      {
+        const uint32_t sa = tmem + sbuf * kSBuf + lane_addr;
+        int r = 0;
+#pragma unroll
+        for (; r + 8 <= kStageR; r += 8) tmem_ld_16x256b_x8(sa + 8 * r, *reinterpret_cast<uint32_t(*)[32]>(sr + 4 * r));
+        if (r + 4 <= kStageR) {
+          tmem_ld_16x256b_x4(sa + 8 * r, sr + 4 * r);
+          r += 4;
+        }
+        if (r + 2 <= kStageR) tmem_ld_16x256b_x2(sa + 8 * r, sr + 4 * r);
+      }
+      // The flags are read before S is released (the K producer relies on it).
+      int blk_ok = 0;
+#pragma unroll
+      for (int b = 0; b < kStageBlocks; ++b) blk_ok |= (sh->blk[fs][b] != 0) << b;
+      tmem_wait_ld();
+      tc_fence_before();
+      warp_arrive(&sh->s_empty[sbuf]);
+      NEB_PHASE(1);
+      const int t0 = cr.lo + s * kStageBlocks;
+      const int nblk = min(kStageBlocks, cr.hi - t0);
+      const int tok0 = t0 * kBlockTokens;
+      // Scores in place (sr holds fp32 bits): scaled into the exp2 domain and
+      // masked to -inf.  Element (r, e) of row a is sr[4r + e], of row b
+      // sr[4r + 2 + e], at token tok0 + 8r + 2*q4 + e.  One copy of the code
+      // serves both rows: row b is swapped into row a's registers and back.
+      float mxa = neg_inf(), mxb = neg_inf();
+      const bool blocks_ok = __all_sync(0xffffffffu, blk_ok == (1 << nblk) - 1);
+#pragma unroll 1
+      for (int x = 0; x < (has_b ? 2 : 1); ++x) {
+        const int lim = (x == 0 ? cr.len_a : cr.len_b) - tok0 - 2 * q4;  // (r, e) valid iff 8r + e < lim
+#pragma unroll
+        for (int r = 0; r < kStageR; ++r)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float v = 8 * r + e < lim ? __uint_as_float(sr[4 * r + e]) * sc : neg_inf();
+            sr[4 * r + e] = __float_as_uint(v);
+          }
+        if (!blocks_ok) {
+#pragma unroll
+          for (int r = 0; r < kStageR; ++r)
+            if (!((blk_ok >> (r >> 1)) & 1)) sr[4 * r] = sr[4 * r + 1] = __float_as_uint(neg_inf());
+        }
+        float t[kStageR];
+#pragma unroll
+        for (int r = 0; r < kStageR; ++r) t[r] = fmaxf(__uint_as_float(sr[4 * r]), __uint_as_float(sr[4 * r + 1]));
+#pragma unroll
+        for (int w2 = kStageR / 2; w2 >= 1; w2 /= 2)
+#pragma unroll
+          for (int r = 0; r < w2; ++r) t[r] = fmaxf(t[r], t[r + w2]);
+        if (x == 0) mxa = t[0]; else mxb = t[0];
+        if (has_b) swap_rows_n<kStageR>(sr);
+      }
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+      if (has_b) {
+        mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+        mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+      }
+      // Lazy rescale: the running max moves only when it grows by more than 8 (x256).
+      float alpha_a = 1.f, alpha_b = 1.f;
+      if (m_a == neg_inf()) {
+        m_a = mxa;
+      } else if (mxa > m_a + 8.f) {
+        alpha_a = fast_exp2(m_a - mxa);
+        m_a = mxa;
+      }
+      if (has_b) {
+        if (m_b == neg_inf()) {
+          m_b = mxb;
+        } else if (mxb > m_b + 8.f) {
+          alpha_b = fast_exp2(m_b - mxb);
+          m_b = mxb;
+        }
+      }
+      NEB_PHASE(2);
+      // P buffer sb is free once PV(G-2) completed.
+      if (G >= 2 && !wait_or_abort(sh, p, &sh->pv_done[sb], (uint32_t)(((G - 2) >> 1) & 1))) {
+        ok = false;
+        break;
+      }
+      if (__any_sync(0xffffffffu, alpha_a != 1.f || alpha_b != 1.f) && s > 0) {
+        if (!wait_or_abort(sh, p, &sh->pv_done[(G - 1) & 1], (uint32_t)(((G - 1) >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        rescale_o(tmem, lane_addr, alpha_a, alpha_b);
+      }
+      // P = 2^(s - m) as fp16 pairs (the MMA operand); rows with nothing
+      // unmasked yet (m = -inf) get zeros.  Row sums come from the tensor core.
+      uint8_t* pbuf = smem + kPOff + sb * kPBuf;
+#pragma unroll 1
+      for (int x = 0; x < (has_b ? 2 : 1); ++x) {
+        const float m = x == 0 ? m_a : m_b;
+        const bool live = m != neg_inf();
+        const int mrow = x == 0 ? ma : mb;
+        uint8_t* prow = pbuf + mrow * 128 + q4 * 4;
+        const int sw = mrow & 7;
+        uint32_t pv[kStageR];
+#pragma unroll
+        for (int r = 0; r < kStageR; ++r)
+          pv[r] = pack_half2(__uint_as_float(sr[4 * r]) - m, __uint_as_float(sr[4 * r + 1]) - m);
+#pragma unroll
+        for (int r = 0; r < kStageR; ++r) pv[r] = live ? ex2_f16x2(pv[r]) : 0u;
+#pragma unroll
+        for (int r = 0; r < kStageR; ++r)
+          *reinterpret_cast<uint32_t*>(prow + (r >> 3) * kPAtom + (((r & 7) ^ sw) << 4)) = pv[r];
+        if (has_b) swap_rows_n<kStageR>(sr);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      warp_arrive(&sh->p_full[sb]);
+      NEB_PHASE(3);
+      if (lane == 0 && G < 100) NEB_TRACE_POINT(c, 608 + 4 * G + (warp - kSoftmaxWarp0));
+    }
+    if (!ok) break;
+    if (!piece_epilogue(c, cr, G - 1, m_a, m_b)) break;
+    have = have_next;
+    cr = nr;
+  }
+  NEB_PHASE_DUMP(c, G);
+}
 
 __global__ void __launch_bounds__(kVThreads, 1)
     verify_attn_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                       const __grid_constant__ VerifyArgs args) {
+                       const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ VerifyArgs args) {
   const AttnParams& p = args.p;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -190,544 +896,95 @@ __global__ void __launch_bounds__(kVThreads, 1)
   int* plan_mem = reinterpret_cast<int*>(smem + kPlanOff);
   __shared__ int scratch[32];
 
+  Ctx c;
+  c.p = &p;
+  c.sh = sh;
+  c.smem = smem;
+  c.trace = nullptr;
+#ifdef NEB_TRACE
+  if (g_trace) c.trace = g_trace + blockIdx.x * 2048;
+#endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) NEB_TRACE_POINT(0);
-  PlanSmem ps{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1)};
-  build_plan(ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, p.max_group_rows);
-  const int ng = ps.misc[0];
-  if (threadIdx.x == 0) NEB_TRACE_POINT(1);
-  const int hk = p.num_kv_heads;
-  const int gqa = p.num_q_heads / p.num_kv_heads;
-  const long long total = (long long)hk * ps.gprefix[ng];
+  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 0);
+  c.ps = PlanSmem{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1)};
+  build_plan(c.ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, p.max_group_rows);
+  c.ng = c.ps.misc[0];
+  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 1);
+  c.hk = p.num_kv_heads;
+  c.gqa = p.num_q_heads / p.num_kv_heads;
+  c.oob_row = args.oob_row;
+  c.total = (long long)c.hk * c.ps.gprefix[c.ng];
   const long long launched = gridDim.x;
-  const long long w = blockIdx.x;
-  if (warp >= kSoftmaxWarp0)
-    write_nan_rows(p, ps, ng, w * 8 + (warp - kSoftmaxWarp0), launched * 8);
-  if (total == 0) return;
-  const long long workers = launched < total ? launched : total;
-  if (w >= workers) return;
-  const long long t_begin = range_begin(w, total, workers);
-  const long long t_end = range_begin(w + 1, total, workers);
+  c.w = blockIdx.x;
+  if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4)
+    write_nan_rows(p, c.ps, c.ng, c.w * 4 + (warp - kSoftmaxWarp0), launched * 4);
+  if (c.total == 0) return;
+  c.workers = launched < c.total ? launched : c.total;
+  if (c.w >= c.workers) return;
+  c.t_begin = range_begin(c.w, c.total, c.workers);
+  c.t_end = range_begin(c.w + 1, c.total, c.workers);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&sh->kv_full[i], 1);
+    for (int i = 0; i < kRing; ++i) {
       mbar_init(&sh->k_full[i], 1);
-      mbar_init(&sh->v_full[i], 1);
       mbar_init(&sh->k_empty[i], 1);
-      mbar_init(&sh->kv_empty[i], 1);
+      mbar_init(&sh->v_full[i], 1);
+      mbar_init(&sh->v_empty[i], 1);
+    }
+    for (int i = 0; i < kFlagSlots; ++i) mbar_init(&sh->flags_full[i], 1);
+    for (int i = 0; i < kSBufs; ++i) {
+      mbar_init(&sh->s_full[i], 1);
+      mbar_init(&sh->s_empty[i], 4);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sh->s_full[i], 1);
-      mbar_init(&sh->s_empty[i], 8);
-      mbar_init(&sh->p_full[i], 8);
+      mbar_init(&sh->p_full[i], 4);
       mbar_init(&sh->pv_done[i], 1);
+      mbar_init(&sh->q_full[i], 1);
+      mbar_init(&sh->q_empty[i], 1);
     }
-    mbar_init(&sh->q_full, 8);
-    mbar_init(&sh->q_empty, 1);
-    mbar_init(&sh->o_empty, 8);
-    mbar_init(&sh->mma_final, 1);
-    mbar_init(&sh->epi_bar, 8);
+    mbar_init(&sh->o_empty, 4);
+    mbar_init(&sh->s_final, 1);
+    mbar_init(&sh->pv_final, 1);
     sh->abort_flag = 0;
-    sh->last_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == kSWarp) {
     tmem_alloc(&sh->tmem_base, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = sh->tmem_base;
-  if (threadIdx.x == 0) NEB_TRACE_POINT(2);
-  const uint32_t q_base = smem_u32(smem + kQOff);
-  const uint32_t kv_base = smem_u32(smem + kKVOff);
-  const uint32_t p_base = smem_u32(smem + kPOff);
+  c.tmem = sh->tmem_base;
+  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 2);
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    // The whole warp looks up 32 block ids at a time (one coalesced read of the
-    // block table); lane 0 waits for free slots and issues the copies.
-    if (lane == 0) {
-      tma_prefetch_desc(&tmap_k);
-      tma_prefetch_desc(&tmap_v);
-    }
-    PieceCursor cur;
-    cur.init(&ps, ng, hk, t_begin, t_end);
-    int g, h, lo, hi, nb;
-    long long ustart;
-    long long G = 0;
-    bool ok = true;
-    while (ok && cur.next(g, h, lo, hi, nb, ustart)) {
-      const int sid = p.seq_ids[ps.gfirst[g]];
-      for (int base = lo; base < hi && ok; base += 32) {
-        const int tile = base + lane;
-        int my_row = args.oob_row, my_valid = 0;
-        if (tile < hi) {
-          const long long blk = lookup_block(p, sid, tile);
-          if (blk >= 0) {
-            my_valid = 1;
-            my_row = (int)(((blk * p.num_layers + p.cur_layer) * hk + h) * kBlockTokens);
-          }
-        }
-        const int nt = min(32, hi - base);
-        for (int s0 = 0; s0 < nt; s0 += kStageBlocks, ++G) {
-          const int nblk = min(kStageBlocks, nt - s0);
-          const int slot = (int)(G % kStages);
-          const uint32_t ph = (uint32_t)(((G / kStages) & 1) ^ 1);
-          int rows[kStageBlocks], valid[kStageBlocks];
-#pragma unroll
-          for (int b = 0; b < kStageBlocks; ++b) {
-            rows[b] = __shfl_sync(0xffffffffu, my_row, s0 + b);
-            valid[b] = __shfl_sync(0xffffffffu, my_valid, s0 + b);
-          }
-          int waited = 1;
-          if (lane == 0) {
-            uint8_t* kst = smem + kKVOff + slot * kStageBytes;
-            // K first: its slot frees as soon as S of the stage G-kStages is done.
-            waited = wait_or_abort(sh, p, &sh->k_empty[slot], ph);
-            if (waited) {
-              if (G < 100) NEB_TRACE_POINT(8 + G);
-              mbar_arrive_expect_tx(&sh->k_full[slot], (uint32_t)nblk * 2u * 2048u);
-              for (int b = 0; b < nblk; ++b) {
-                tma_load_2d(kst + b * 2048, &tmap_k, &sh->k_full[slot], 0, rows[b]);
-                tma_load_2d(kst + 8192 + b * 2048, &tmap_k, &sh->k_full[slot], 64, rows[b]);
-              }
-              waited = wait_or_abort(sh, p, &sh->kv_empty[slot], ph);
-            }
-            if (waited) {
-              if (G < 100) NEB_TRACE_POINT(508 + G);
-              mbar_arrive_expect_tx(&sh->v_full[slot], (uint32_t)nblk * 2u * 2048u);
-              for (int b = 0; b < nblk; ++b) {
-                tma_load_2d(kst + 16384 + b * 2048, &tmap_v, &sh->v_full[slot], 0, rows[b]);
-                tma_load_2d(kst + 16384 + 8192 + b * 2048, &tmap_v, &sh->v_full[slot], 64, rows[b]);
-              }
-              // The flags of stage G go in only now: the softmax of stage G - kStages,
-              // the previous reader of this slot, finished before its P V completed.
-              for (int b = 0; b < nblk; ++b) sh->blk[slot][b] = valid[b];
-              mbar_arrive(&sh->kv_full[slot]);
-            }
-          }
-          waited = __shfl_sync(0xffffffffu, waited, 0);
-          if (!waited) {
-            ok = false;
-            break;
-          }
-          __syncwarp();
-        }
-      }
-    }
-    // Wait (bounded) for every copy this CTA issued before the CTA can exit.
-    if (lane == 0)
-      for (long long Gi = (G > kStages ? G - kStages : 0); Gi < G; ++Gi) {
-        mbar_wait(&sh->k_full[Gi % kStages], (uint32_t)((Gi / kStages) & 1), kWaitLimit);
-        mbar_wait(&sh->v_full[Gi % kStages], (uint32_t)((Gi / kStages) & 1), kWaitLimit);
-      }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------- MMA issuer
-    // Polls the barriers and issues whichever is ready first: S(G) for the next
-    // stage, or O += P V for the oldest stage whose P is written.  Up to two
-    // P V products may be pending, so neither waits for the other's inputs.
-    if (lane == 0) {
-      PieceCursor cur;
-      cur.init(&ps, ng, hk, t_begin, t_end);
-      int g, h, lo, hi, nb;
-      long long ustart;
-      int piece = -1, s_in_piece = 0, nst = 0;
-      struct Stage {
-        int nblk, first, last, piece;
-      };
-      auto next_stage = [&](Stage& st) -> bool {
-        if (s_in_piece == nst) {
-          if (!cur.next(g, h, lo, hi, nb, ustart)) return false;
-          ++piece;
-          nst = stages_of(lo, hi);
-          s_in_piece = 0;
-        }
-        st.nblk = min(kStageBlocks, hi - (lo + s_in_piece * kStageBlocks));
-        st.first = s_in_piece == 0;
-        st.last = s_in_piece == nst - 1;
-        st.piece = piece;
-        ++s_in_piece;
-        return true;
-      };
-      const uint32_t idesc_pv = idesc_f16_f32(128, 128, false, true);
-      const uint32_t idesc_sum = idesc_f16_f32(128, 16, false, false);
-      const uint32_t ones_base = smem_u32(smem + kOnesOff);
-      Stage nxt, pend[2];
-      long long pend_g[2] = {0, 0};
-      int npend = 0, phead = 0;
-      bool have = next_stage(nxt);
-      long long Gs = 0;
-      long long t_idle = clock64();
-      while (have || npend > 0) {
-        bool progress = false;
-        if (npend > 0) {
-          const Stage& st = pend[phead];
-          const long long Gp = pend_g[phead];
-          bool ready = mbar_test_wait(&sh->p_full[Gp & 1], (uint32_t)((Gp >> 1) & 1)) &&
-                       mbar_test_wait(&sh->v_full[Gp % kStages], (uint32_t)((Gp / kStages) & 1));
-          if (ready && st.first && st.piece > 0) ready = mbar_test_wait(&sh->o_empty, (uint32_t)((st.piece - 1) & 1));
-          if (ready) {
-            if (Gp < 100) NEB_TRACE_POINT(208 + Gp);
-            tc_fence_after();
-            const int sb = (int)(Gp & 1), slot = (int)(Gp % kStages);
-            const uint32_t vst = kv_base + slot * kStageBytes + 16384;
-            for (int kb = 0; kb < st.nblk; ++kb) {
-              const uint64_t a = smem_desc_sw128(p_base + sb * 16384 + kb * 32, 16, 1024);
-              const uint64_t b = smem_desc_sw128(vst + kb * 2048, 8192, 1024);
-              const uint32_t acc = (st.first && kb == 0) ? 0u : 1u;
-              mma_f16(tmem + kOCol, a, b, idesc_pv, acc);
-              mma_f16(tmem + kSumCol, a, smem_desc_sw128(ones_base + (kb & 3) * 32, 16, 1024), idesc_sum, acc);
-            }
-            mma_commit(&sh->kv_empty[slot]);
-            mma_commit(&sh->pv_done[sb]);
-            phead ^= 1;
-            --npend;
-            progress = true;
-          }
-        }
-        if (have && npend < 2) {
-          bool ready = true;
-          if (nxt.first) ready = mbar_test_wait(&sh->q_full, (uint32_t)(nxt.piece & 1));
-          ready = ready && mbar_test_wait(&sh->k_full[Gs % kStages], (uint32_t)((Gs / kStages) & 1)) &&
-                  mbar_test_wait(&sh->s_empty[Gs & 1], (uint32_t)(((Gs >> 1) & 1) ^ 1));
-          if (ready) {
-            if (Gs < 100) NEB_TRACE_POINT(108 + Gs);
-            tc_fence_after();
-            const int sb = (int)(Gs & 1);
-            const uint32_t idesc_s = idesc_f16_f32(128, 16 * nxt.nblk, false, false);
-            const uint32_t kst = kv_base + (int)(Gs % kStages) * kStageBytes;
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t a = smem_desc_sw128(q_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-              const uint64_t b = smem_desc_sw128(kst + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-              mma_f16(tmem + sb * 64, a, b, idesc_s, kk > 0 ? 1u : 0u);
-            }
-            mma_commit(&sh->s_full[sb]);
-            mma_commit(&sh->k_empty[Gs % kStages]);
-            if (nxt.last) mma_commit(&sh->q_empty);
-            const int slot_in = (phead + npend) & 1;
-            pend[slot_in] = nxt;
-            pend_g[slot_in] = Gs;
-            ++npend;
-            ++Gs;
-            have = next_stage(nxt);
-            progress = true;
-          }
-        }
-        if (progress) {
-          t_idle = clock64();
-        } else if (aborted(sh) || clock64() - t_idle > kWaitLimit) {
-          raise_abort(sh, p);
-          break;
-        } else {
-          // Back off: a tight poll of the barriers competes with the softmax
-          // warps for the shared-memory pipe.
-          __nanosleep(40);
-        }
-      }
-      mma_commit(&sh->mma_final);
-      mbar_wait(&sh->mma_final, 0, kWaitLimit);
-    }
-  } else if (warp >= kSoftmaxWarp0) {
-    // ------------------------------------------------- softmax and epilogue
-    const int tid = threadIdx.x - kSoftmaxWarp0 * 32;  // 0..255
-    const int wg = (warp - kSoftmaxWarp0) >> 2;          // warpgroup: which 16-lane half of the quadrant
-    const int qd = warp & 3;                             // TMEM lane quadrant of this warp
-    const int q4 = lane & 3;
-    const int li_a = lane >> 2, li_b = li_a + 8;           // lanes within the warpgroup's half
-    const int ja = (2 * li_a + wg) * 4 + qd, jb = (2 * li_b + wg) * 4 + qd;  // unit query rows
-    const int ma = qd * 32 + wg * 16 + li_a, mb = ma + 8;  // MMA rows
-    const uint32_t lane_addr = (uint32_t)(qd * 32 + wg * 16) << 16;
-    // Clear Q and P once: rows no unit writes must hold finite values.
-    for (int i = tid; i < (32768 + 32768) / 16; i += kSoftmaxThreads) {
-      uint8_t* dst = i < 2048 ? smem + kQOff + i * 16 : smem + kPOff + (i - 2048) * 16;
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-    }
-    named_bar_sync(1, kSoftmaxThreads);
-    for (int i = tid; i < 2048 / 16; i += kSoftmaxThreads)
-      *reinterpret_cast<uint4*>(smem + kOnesOff + i * 16) = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
-    PieceCursor cur;
-    cur.init(&ps, ng, hk, t_begin, t_end);
-    int g, h, lo, hi, nb;
-    long long ustart;
-    auto load_q = [&](int grp, int kv_head) {
-      const int first_row = ps.gfirst[grp];
-      const int nq = (ps.gfirst[grp + 1] - first_row) * gqa;
-      for (int i = tid; i < nq * 16; i += kSoftmaxThreads) {
-        const int j = i >> 4, c = i & 15;
-        const int row = first_row + j / gqa;
-        const int head = kv_head * gqa + j % gqa;
-        uint4 v = *reinterpret_cast<const uint4*>(p.q + ((long long)row * p.num_q_heads + head) * kHeadDim + c * 8);
-        // Fold softmax_scale * log2(e) into Q: S then comes out in the exp2 domain.
-        uint32_t* w4 = reinterpret_cast<uint32_t*>(&v);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = h2_to_f2(w4[e]);
-          w4[e] = pack_half2(f.x * p.scale_log2, f.y * p.scale_log2);
-        }
-        const int m = (j & 3) * 32 + ((j >> 2) & 1) * 16 + (j >> 3);
-        uint8_t* dst = smem + kQOff + (c >> 3) * 16384 + m * 128 + (((c & 7) ^ (m & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = v;
-      }
-      fence_proxy_async_smem();
-      warp_arrive(&sh->q_full);
-    };
-    bool have = cur.next(g, h, lo, hi, nb, ustart);
-    if (have) load_q(g, h);
-    long long G = 0;
-    int pi = 0;
-    uint32_t epi_phase = 0;
-    bool ok = true;
-    while (have && ok) {
-      const int first_row = ps.gfirst[g];
-      const int nrows = ps.gfirst[g + 1] - first_row;
-      const int nq = nrows * gqa;
-      const int len_a = ja < nq ? p.seq_lens[first_row + ja / gqa] : -1;
-      const int len_b = jb < nq ? p.seq_lens[first_row + jb / gqa] : -1;
-      // Warp-uniform: does any lane of this warp own a second query row?
-      const bool has_b = __any_sync(0xffffffffu, jb < nq);
-      float m_a = neg_inf(), m_b = neg_inf();
-      const int nst = stages_of(lo, hi);
-      for (int s = 0; s < nst; ++s, ++G) {
-        const int slot = (int)(G % kStages);
-        const int sb = (int)(G & 1);
-        if (!wait_or_abort(sh, p, &sh->kv_full[slot], (uint32_t)((G / kStages) & 1)) ||
-            !wait_or_abort(sh, p, &sh->s_full[sb], (uint32_t)((G >> 1) & 1))) {
-          ok = false;
-          break;
-        }
-        if (tid == 0 && G < 100) NEB_TRACE_POINT(308 + G);
-        tc_fence_after();
-        uint32_t sr[32];
-        tmem_ld_16x256b_x8(tmem + sb * 64 + lane_addr, sr);
-        tmem_wait_ld();
-        tc_fence_before();
-        warp_arrive(&sh->s_empty[sb]);
-        const int t0 = lo + s * kStageBlocks;
-        const int nblk = min(kStageBlocks, hi - t0);
-        const int tok0 = t0 * kBlockTokens;
-        float xa[16], xb[16];
-        float mxa = neg_inf(), mxb = neg_inf();
-        // Interior stages (every block present, every token below both rows'
-        // lengths, or the row absent) need no per-element mask.
-        bool blocks_ok = true;
-        for (int b = 0; b < nblk; ++b) blocks_ok = blocks_ok && sh->blk[slot][b] != 0;
-        const int tok_end = tok0 + 16 * nblk;
-        const bool fast = __all_sync(0xffffffffu, blocks_ok && nblk == kStageBlocks &&
-                                                      (len_a < 0 || tok_end <= len_a) && (len_b < 0 || tok_end <= len_b));
-        if (fast && !has_b) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            xa[i] = len_a >= 0 ? __uint_as_float(sr[4 * (i >> 1) + (i & 1)]) : neg_inf();
-            mxa = fmaxf(mxa, xa[i]);
-          }
-        } else if (fast) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int r = i >> 1, e = i & 1;
-            xa[i] = len_a >= 0 ? __uint_as_float(sr[4 * r + e]) : neg_inf();
-            xb[i] = len_b >= 0 ? __uint_as_float(sr[4 * r + 2 + e]) : neg_inf();
-            mxa = fmaxf(mxa, xa[i]);
-            mxb = fmaxf(mxb, xb[i]);
-          }
-        } else {
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const bool blk_ok = (r >> 1) < nblk && sh->blk[slot][r >> 1] != 0;
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int tok = tok0 + 8 * r + 2 * q4 + e;
-              const bool va = blk_ok && tok < len_a;
-              const bool vb = blk_ok && tok < len_b;
-              xa[2 * r + e] = va ? __uint_as_float(sr[4 * r + e]) : neg_inf();
-              xb[2 * r + e] = vb ? __uint_as_float(sr[4 * r + 2 + e]) : neg_inf();
-              mxa = fmaxf(mxa, xa[2 * r + e]);
-              mxb = fmaxf(mxb, xb[2 * r + e]);
-            }
-          }
-        }
-        mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
-        mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
-        if (has_b) {
-          mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
-          mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
-        }
-        // Lazy rescale: the running max moves only when it grows by more than 8 (x256).
-        float alpha_a = 1.f, alpha_b = 1.f;
-        if (m_a == neg_inf()) {
-          m_a = mxa;
-        } else if (mxa > m_a + 8.f) {
-          alpha_a = fast_exp2(m_a - mxa);
-          m_a = mxa;
-        }
-        if (m_b == neg_inf()) {
-          m_b = mxb;
-        } else if (mxb > m_b + 8.f) {
-          alpha_b = fast_exp2(m_b - mxb);
-          m_b = mxb;
-        }
-        // P = 2^(s - m) in fp16 pairs (the MMA operand); rows with nothing
-        // unmasked yet (m = -inf) get zeros.  Row sums come from the tensor core.
-        uint32_t pa[8], pb[8];
-        const bool live_a = m_a != neg_inf(), live_b = m_b != neg_inf();
-#pragma unroll
-        for (int r = 0; r < 8; ++r) pa[r] = live_a ? ex2_f16x2(pack_half2(xa[2 * r] - m_a, xa[2 * r + 1] - m_a)) : 0u;
-        if (has_b) {
-#pragma unroll
-          for (int r = 0; r < 8; ++r) pb[r] = live_b ? ex2_f16x2(pack_half2(xb[2 * r] - m_b, xb[2 * r + 1] - m_b)) : 0u;
-        }
-        // P buffer sb is free once PV(G-2) completed.
-        if (G >= 2 && !wait_or_abort(sh, p, &sh->pv_done[sb], (uint32_t)(((G - 2) >> 1) & 1))) {
-          ok = false;
-          break;
-        }
-        const bool rescale = __any_sync(0xffffffffu, alpha_a != 1.f || alpha_b != 1.f) && s > 0;
-        if (rescale) {
-          if (!wait_or_abort(sh, p, &sh->pv_done[(G - 1) & 1], (uint32_t)(((G - 1) >> 1) & 1))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t orr[32];
-            const uint32_t oaddr = tmem + kOCol + half * 64 + lane_addr;
-            tmem_ld_16x256b_x8(oaddr, orr);
-            tmem_wait_ld();
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              orr[4 * r + 0] = __float_as_uint(__uint_as_float(orr[4 * r + 0]) * alpha_a);
-              orr[4 * r + 1] = __float_as_uint(__uint_as_float(orr[4 * r + 1]) * alpha_a);
-              orr[4 * r + 2] = __float_as_uint(__uint_as_float(orr[4 * r + 2]) * alpha_b);
-              orr[4 * r + 3] = __float_as_uint(__uint_as_float(orr[4 * r + 3]) * alpha_b);
-            }
-            tmem_st_16x256b_x8(oaddr, orr);
-          }
-          uint32_t srr[8];
-          tmem_ld_16x256b_x2(tmem + kSumCol + lane_addr, srr);
-          tmem_wait_ld();
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            srr[4 * r + 0] = __float_as_uint(__uint_as_float(srr[4 * r + 0]) * alpha_a);
-            srr[4 * r + 1] = __float_as_uint(__uint_as_float(srr[4 * r + 1]) * alpha_a);
-            srr[4 * r + 2] = __float_as_uint(__uint_as_float(srr[4 * r + 2]) * alpha_b);
-            srr[4 * r + 3] = __float_as_uint(__uint_as_float(srr[4 * r + 3]) * alpha_b);
-          }
-          tmem_st_16x256b_x2(tmem + kSumCol + lane_addr, srr);
-          tmem_wait_st();
-        }
-        uint8_t* pbuf = smem + kPOff + sb * 16384;
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-          *reinterpret_cast<uint32_t*>(pbuf + ma * 128 + ((r ^ (ma & 7)) << 4) + q4 * 4) = pa[r];
-        if (has_b) {
-#pragma unroll
-          for (int r = 0; r < 8; ++r)
-            *reinterpret_cast<uint32_t*>(pbuf + mb * 128 + ((r ^ (mb & 7)) << 4) + q4 * 4) = pb[r];
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        warp_arrive(&sh->p_full[sb]);
-        if (tid == 0 && G < 100) NEB_TRACE_POINT(408 + G);
-      }
-      if (!ok) break;
-      // Load the next piece's Q as soon as this piece's S products are done with it.
-      int g2, h2, lo2, hi2, nb2;
-      long long ustart2;
-      const bool have_next = cur.next(g2, h2, lo2, hi2, nb2, ustart2);
-      if (have_next) {
-        if (!wait_or_abort(sh, p, &sh->q_empty, (uint32_t)(pi & 1))) break;
-        load_q(g2, h2);
-      }
-      // Epilogue of this piece.
-      const long long Gl = G - 1;
-      if (!wait_or_abort(sh, p, &sh->pv_done[Gl & 1], (uint32_t)((Gl >> 1) & 1))) break;
-      tc_fence_after();
-      uint32_t o0[32], o1[32], sums[8];
-      tmem_ld_16x256b_x8(tmem + kOCol + lane_addr, o0);
-      tmem_ld_16x256b_x8(tmem + kOCol + 64 + lane_addr, o1);
-      tmem_ld_16x256b_x2(tmem + kSumCol + lane_addr, sums);
-      tmem_wait_ld();
-      tc_fence_before();
-      warp_arrive(&sh->o_empty);
-      const float l_a = __uint_as_float(sums[0]), l_b = __uint_as_float(sums[2]);
-      const float inv_a = 1.f / l_a, inv_b = 1.f / l_b;
-      const bool whole = (lo == 0 && hi == nb);
-      const long long unit = (long long)g * hk + h;
-      long long w0 = 0, w1 = 0, slot = 0;
-      if (!whole) {
-        w0 = worker_of(ustart, total, workers);
-        w1 = worker_of(ustart + nb - 1, total, workers);
-        slot = piece_slot(w, w0);
-      }
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        const int j = x == 0 ? ja : jb;
-        if (j >= nq) continue;
-        const float inv = x == 0 ? inv_a : inv_b;
-        const int row = first_row + j / gqa;
-        const int head = h * gqa + j % gqa;
-        if (whole) {
-          __half* dst = p.o + ((long long)row * p.num_q_heads + head) * kHeadDim;
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const int d = 8 * r + 2 * q4;
-            *reinterpret_cast<uint32_t*>(dst + d) =
-                pack_half2(__uint_as_float(o0[4 * r + 2 * x]) * inv, __uint_as_float(o0[4 * r + 2 * x + 1]) * inv);
-            *reinterpret_cast<uint32_t*>(dst + 64 + d) =
-                pack_half2(__uint_as_float(o1[4 * r + 2 * x]) * inv, __uint_as_float(o1[4 * r + 2 * x + 1]) * inv);
-          }
-        } else {
-          float* dst = p.part_o + (slot * p.nq + j) * kHeadDim;
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const int d = 8 * r + 2 * q4;
-            __stcg(reinterpret_cast<float2*>(dst + d),
-                   make_float2(__uint_as_float(o0[4 * r + 2 * x]) * inv, __uint_as_float(o0[4 * r + 2 * x + 1]) * inv));
-            __stcg(reinterpret_cast<float2*>(dst + 64 + d),
-                   make_float2(__uint_as_float(o1[4 * r + 2 * x]) * inv, __uint_as_float(o1[4 * r + 2 * x + 1]) * inv));
-          }
-          if (q4 == 0) {
-            const float l = x == 0 ? l_a : l_b;
-            const float m = x == 0 ? m_a : m_b;
-            __stcg(p.part_lse + slot * p.nq + j, l > 0.f ? m + __log2f(l) : neg_inf());
-          }
-        }
-      }
-      if (!whole) {
-        __threadfence();
-        if (!epi_sync(sh, p, epi_phase)) break;
-        if (tid == 0) {
-          const int last = atomicAdd(p.counters + unit, 1) == (int)(w1 - w0);
-          if (last) p.counters[unit] = 0;  // every piece has arrived: ready for the next call
-          sh->last_flag = last;
-        }
-        if (!epi_sync(sh, p, epi_phase)) break;
-        if (sh->last_flag) {
-          __threadfence();
-          merge_unit_warp(p, first_row, nrows, h, gqa, w0, w1, warp - kSoftmaxWarp0, 8);
-        }
-      }
-      have = have_next;
-      g = g2; h = h2; lo = lo2; hi = hi2; nb = nb2; ustart = ustart2;
-      ++pi;
-    }
+  if (warp == kKWarp) {
+    producer(c, &tmap_k, sh->k_full, sh->k_empty, kKOff, 1);
+  } else if (warp == kVWarp) {
+    producer(c, &tmap_v, sh->v_full, sh->v_empty, kVOff, 0);
+  } else if (warp == kSWarp) {
+    if (lane == 0) s_issuer(c, &tmap_q);
+  } else if (warp == kPVWarp) {
+    if (lane == 0) pv_issuer(c);
+  } else {
+    softmax_role(c);
+    if (warp == kSoftmaxWarp0 && lane == 0) NEB_TRACE_POINT(c, 3);
   }
-  if (warp == 2 && lane == 0) NEB_TRACE_POINT(3);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
-  if (threadIdx.x == 0) NEB_TRACE_POINT(4);
+  if (warp == kSWarp) tmem_dealloc(c.tmem, kTmemCols);
+  if (!aborted(sh)) finish_split_units(c, scratch);
+  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 4);
 }
 
 // ------------------------------------------------------------------ host side
 long long verify_workers(int device) { return num_sms(device); }
 
+int verify_max_rows() { return kVerifyMaxRows; }
+
 int verify_group_rows(int gqa) {
-  if (gqa < 1 || gqa > 64) return 0;
+  if (gqa < 1 || gqa > kMaxGqa) return 0;
   return kMaxQRows / gqa;
 }
 
@@ -744,54 +1001,88 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Tensor map over a cache viewed as [rows = NB*L*Hk*16, 128] fp16 with 64x16 boxes.
-static int kv_tensor_map(CUtensorMap* map, const void* base, unsigned long long rows) {
+// fp16 tensor map with 128-byte swizzle, cached by its full description.
+static int tensor_map(CUtensorMap* map, const void* base, int rank, const unsigned long long* dims,
+                      const unsigned long long* strides, const unsigned* box) {
   struct Entry {
     const void* base;
-    unsigned long long rows;
+    int rank;
+    unsigned long long dims[3], strides[2];
+    unsigned box[3];
     CUtensorMap map;
   };
   static std::mutex mu;
-  static Entry cache[16];
+  static Entry cache[32];
   static int next = 0;
+  auto same = [&](const Entry& e) {
+    if (e.base != base || e.rank != rank) return false;
+    for (int i = 0; i < rank; ++i)
+      if (e.dims[i] != dims[i] || e.box[i] != box[i] || (i + 1 < rank && e.strides[i] != strides[i])) return false;
+    return true;
+  };
   {
     std::lock_guard<std::mutex> lock(mu);
     for (auto& e : cache)
-      if (e.base == base && e.rows == rows) {
+      if (same(e)) {
         *map = e.map;
         return NEB_OK;
       }
   }
   auto fn = encode_fn();
   NEB_REQUIRE(fn != nullptr, NEB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[2] = {128, rows};
-  cuuint64_t strides[1] = {256};
-  cuuint32_t box[2] = {64, 16};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  cuuint64_t d[3] = {0, 0, 0}, st[2] = {0, 0};
+  cuuint32_t bx[3] = {0, 0, 0}, estr[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), d, st, bx, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   NEB_REQUIRE(r == CUDA_SUCCESS, NEB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   std::lock_guard<std::mutex> lock(mu);
-  cache[next] = Entry{base, rows, *map};
-  next = (next + 1) % 16;
+  Entry& e = cache[next];
+  e.base = base;
+  e.rank = rank;
+  for (int i = 0; i < 3; ++i) {
+    e.dims[i] = i < rank ? dims[i] : 0;
+    e.box[i] = i < rank ? box[i] : 0;
+    if (i < 2) e.strides[i] = i + 1 < rank ? strides[i] : 0;
+  }
+  e.map = *map;
+  next = (next + 1) % 32;
   return NEB_OK;
 }
 
 int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream) {
+  const int gqa = p.num_q_heads / p.num_kv_heads;
   const unsigned long long rows =
       (unsigned long long)p.num_blocks * p.num_layers * p.num_kv_heads * kBlockTokens;
   NEB_REQUIRE(rows + kBlockTokens < (1ull << 31), NEB_ERR_UNSUPPORTED,
               "KV cache of %llu rows exceeds the verify kernel's 2^31-row tensor map", rows);
   NEB_REQUIRE(p.num_rows <= kVerifyMaxRows, NEB_ERR_UNSUPPORTED,
               "verify attention takes at most %d rows per call (got %d)", kVerifyMaxRows, p.num_rows);
-  NEB_REQUIRE(p.max_group_rows * (p.num_q_heads / p.num_kv_heads) <= kMaxQRows, NEB_ERR_INVALID,
+  NEB_REQUIRE(gqa >= 1 && gqa <= kMaxGqa && p.max_group_rows * gqa <= kMaxQRows, NEB_ERR_INVALID,
               "group rows exceed the MMA tile");
-  CUtensorMap tk, tv;
-  int rc = kv_tensor_map(&tk, p.k_cache, rows);
-  if (rc != NEB_OK) return rc;
-  rc = kv_tensor_map(&tv, p.v_cache, rows);
-  if (rc != NEB_OK) return rc;
+  NEB_REQUIRE((reinterpret_cast<uintptr_t>(p.q) & 15u) == 0, NEB_ERR_INVALID, "q must be 16-byte aligned");
+  CUtensorMap tk, tv, tq;
+  {
+    const unsigned long long dims[2] = {128, rows}, strides[1] = {256};
+    const unsigned box[2] = {64, 16};
+    int rc = tensor_map(&tk, p.k_cache, 2, dims, strides, box);
+    if (rc != NEB_OK) return rc;
+    rc = tensor_map(&tv, p.v_cache, 2, dims, strides, box);
+    if (rc != NEB_OK) return rc;
+  }
+  {
+    // Q as [rows][q heads][128]: a box is one query chunk, gqa heads x (16 / gqa) rows.
+    const unsigned long long dims[3] = {128, (unsigned long long)p.num_q_heads, (unsigned long long)p.num_rows};
+    const unsigned long long strides[2] = {256, 256ull * p.num_q_heads};
+    const unsigned box[3] = {64, (unsigned)gqa, (unsigned)(16 / gqa)};
+    int rc = tensor_map(&tq, p.q, 3, dims, strides, box);
+    if (rc != NEB_OK) return rc;
+  }
   VerifyArgs a;
   a.p = p;
   a.oob_row = (int)rows;
@@ -809,7 +1100,7 @@ int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream) {
       attr_set[device] = true;
     }
   }
-  verify_attn_kernel<<<(unsigned)workers, kVThreads, smem, stream>>>(tk, tv, a);
+  verify_attn_kernel<<<(unsigned)workers, kVThreads, smem, stream>>>(tk, tv, tq, a);
   NEB_CUDA(cudaGetLastError());
   return NEB_OK;
 }

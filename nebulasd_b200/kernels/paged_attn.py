@@ -42,11 +42,14 @@ def get_kernel() -> str:
 VERIFY_BUILT = os.environ.get("NEB_VERIFY_BUILT", "1") == "1"
 
 
-def choose_kernel(num_q_heads: int, num_kv_heads: int) -> int:
+def choose_kernel(num_q_heads: int, num_kv_heads: int, num_rows: int = 0) -> int:
+    """Tensor-core kernel for GQA ratios 4..16 (the rows x heads of a request
+    fill its MMA tiles) up to its row limit; the CUDA-core kernel otherwise."""
     forced = _MODES[_mode]
     if forced is not None:
         return forced
-    if VERIFY_BUILT and num_q_heads // num_kv_heads >= 4:
+    gqa = num_q_heads // num_kv_heads
+    if VERIFY_BUILT and 4 <= gqa <= 16 and num_rows <= _lib.lib.neb_attention_max_rows(_lib.NEB_ATTN_VERIFY):
         return _lib.NEB_ATTN_VERIFY
     return _lib.NEB_ATTN_DECODE
 
@@ -78,7 +81,7 @@ def paged_attention_raw(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
     if o.shape != q.shape or seq_lens.shape[0] != num_rows or seq_ids.shape[0] != num_rows:
         raise ValueError("q, o, seq_lens and seq_ids disagree on the number of rows")
     if kernel is None:
-        kernel = choose_kernel(num_q_heads, num_kv_heads)
+        kernel = choose_kernel(num_q_heads, num_kv_heads, num_rows)
     stream = stream or torch.cuda.current_stream(q.device)
     if workspace is None:
         workspace = attention_workspace(kernel, q.device, stream, num_rows, num_q_heads, num_kv_heads)
