@@ -81,6 +81,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long l
   return true;
 }
 
+// Load of a counter other CTAs update, with acquire semantics at GPU scope.
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
 // ---------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");

@@ -116,10 +116,13 @@ struct VerifyShared {
   uint64_t q_full[2];
   uint64_t q_empty[2];
   uint64_t o_empty;
+  uint64_t part_ready;           // softmax wrote the partial of the CTA's first piece (split, not last)
   uint64_t s_final;
   uint64_t pv_final;
   uint32_t tmem_base;
   int32_t abort_flag;
+  int32_t merge_mode;            // epilogue of the last piece: merge directly with the other partial
+  int32_t first_last;            // the first piece's count completed its unit: merge it at the end
   int32_t blk[kFlagSlots][kStageBlocks];
 };
 static_assert(sizeof(VerifyShared) <= 1024, "barrier block fits its slot");
@@ -353,6 +356,41 @@ struct TileFeed {
   }
 };
 
+// The first piece of a worker's range, when it is part of a unit split across
+// CTAs and not the worker's only piece: the K warp counts its partial in as
+// soon as the softmax has written it, so that the CTA finishing the unit's
+// other part (late, as its last piece) finds it in and merges directly.
+struct FirstSplit {
+  bool pending;
+  long long unit, w0, w1;
+  int g, h;
+  __device__ __noinline__ void init(const Ctx& c) {
+    PieceCursor cur;
+    cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+    int lo, hi, nb;
+    long long ustart;
+    pending = false;
+    if (!cur.next(g, h, lo, hi, nb, ustart)) return;
+    if ((lo == 0 && hi == nb) || c.t_begin + (hi - lo) >= c.t_end) return;
+    pending = true;
+    unit = (long long)g * c.hk + h;
+    w0 = worker_of(ustart, c.total, c.workers);
+    w1 = worker_of(ustart + nb - 1, c.total, c.workers);
+  }
+  // Lane-0 work once the softmax has arrived: publish the partial and count it.
+  __device__ __noinline__ void count(const Ctx& c) {
+    // The mbarrier wait ordered the softmax warps' partial stores before this
+    // fence, which publishes them with the count.
+    __threadfence();
+    const int last = atomicAdd(c.p->counters + unit, 1) == (int)(w1 - w0);
+    if (last) {
+      c.p->counters[unit] = 0;  // every piece has arrived: ready for the next call
+      c.sh->first_last = 1;
+    }
+    pending = false;
+  }
+};
+
 // ------------------------------------------------------------------ producers
 // One function serves the K warp (flags != 0: it also publishes the block
 // flags) and the V warp.  Slot G % kRing frees when the MMA that read it (S for
@@ -362,7 +400,7 @@ struct TileFeed {
 // S(G - kRing) (issued only once S buffer (G - kRing) % kSBufs was released by
 // the softmax of stage G - kRing - kSBufs), and so this load, had to wait for.
 __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uint64_t* full, uint64_t* empty,
-                                      uint32_t ring_off, int flags) {
+                                      uint32_t ring_off, int flags, FirstSplit* first) {
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
   const int lane = threadIdx.x & 31;
@@ -404,6 +442,8 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
           }
         }
       }
+      // The K warp counts the first piece in as soon as its partial is written.
+      if (lane == 0 && first && first->pending && mbar_test_wait(&sh->part_ready, 0)) first->count(c);
       waited = __shfl_sync(0xffffffffu, waited, 0);
       if (!waited) {
         ok = false;
@@ -413,6 +453,7 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
       feed.advance(pos);
     }
   }
+  if (lane == 0 && first && first->pending && wait_or_abort(sh, p, &sh->part_ready, 0)) first->count(c);
   // Wait (bounded) for every copy this warp issued before the CTA can exit.
   if (lane == 0)
 #pragma unroll 1
@@ -420,50 +461,16 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
       mbar_wait(&full[Gi % kRing], (uint32_t)((Gi / kRing) & 1), kWaitLimit);
 }
 
-// After the pipeline has drained, the whole CTA counts its split pieces in
-// (at most two: its first and its last piece) and merges the units it
-// completes.  Every thread has passed a CTA barrier after the softmax warps'
-// partial stores, so one fence per thread publishes them, with the counts, to
-// the other CTAs.
-__device__ __noinline__ void finish_split_units(const Ctx& c, int* flags) {
-  const AttnParams& p = *c.p;
-  PieceCursor cur;
-  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
-  int g[2], h[2], lo, hi, nb;
-  long long us[2], ustart;
-  int k = 0;
-  while (k < 2 && cur.next(g[k], h[k], lo, hi, nb, ustart)) {
-    if (lo == 0 && hi == nb) continue;
-    us[k++] = ustart;
-  }
-  if (k == 0) return;
-  if (threadIdx.x < k) {
-    // The CTA barrier before this call ordered every thread's partial stores
-    // before this fence, which publishes them with the count.
-    __threadfence();
-    const int i = threadIdx.x;
-    const int nbi = c.ps.gprefix[g[i] + 1] - c.ps.gprefix[g[i]];
-    const long long w0 = worker_of(us[i], c.total, c.workers);
-    const long long w1 = worker_of(us[i] + nbi - 1, c.total, c.workers);
-    const long long unit = (long long)g[i] * c.hk + h[i];
-    const int last = atomicAdd(p.counters + unit, 1) == (int)(w1 - w0);
-    if (last) p.counters[unit] = 0;  // every piece has arrived: ready for the next call
-    flags[i] = last;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 1700);
-#pragma unroll 1
-  for (int i = 0; i < k; ++i) {
-    if (!flags[i]) continue;
-    __threadfence();
-    const int nbi = c.ps.gprefix[g[i] + 1] - c.ps.gprefix[g[i]];
-    const long long w0 = worker_of(us[i], c.total, c.workers);
-    const long long w1 = worker_of(us[i] + nbi - 1, c.total, c.workers);
-    const int first_row = c.ps.gfirst[g[i]];
-    merge_unit_threads(p, first_row, c.ps.gfirst[g[i] + 1] - first_row, h[i], c.gqa, w0, w1, threadIdx.x,
-                       kVThreads);
-    if (threadIdx.x == 0) NEB_TRACE_POINT(c, 1701 + i);
-  }
+
+// At the very end, if counting the first piece completed its unit (the other
+// part finished first), the whole CTA merges the unit's partials.
+__device__ __noinline__ void finish_first_unit(const Ctx& c) {
+  FirstSplit fs;
+  fs.init(c);
+  __threadfence();
+  const int first_row = c.ps.gfirst[fs.g];
+  merge_unit_threads(*c.p, first_row, c.ps.gfirst[fs.g + 1] - first_row, fs.h, c.gqa, fs.w0, fs.w1, threadIdx.x,
+                     kVThreads);
 }
 
 // ------------------------------------------------------------------- S issuer
@@ -636,12 +643,19 @@ struct SoftmaxRows {
   int ja, jb, len_a, len_b;  // unit rows (-1: none) and their lengths
 };
 
-// End of a piece: O / l as fp16 output rows, or a partial (O / l, and
-// m + log2 l) for the merge; the PV issuer may reuse O once it is read.
-__device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, int G_last, float m_a, float m_b) {
+// End of a piece: O / l as fp16 output rows, or, for a unit split across
+// CTAs, a partial (O / l and m + log2 l).  The last piece of the CTA's range
+// first looks at the unit's counter: when the one other piece has been counted
+// in already, it merges that partial with its own O directly.  Otherwise it
+// writes its partial and counts it in, and if that completes the unit the
+// softmax warps merge the partials.  The first piece's partial is counted in
+// by the K warp.  The PV issuer may reuse O once it has been read.
+__device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, int G_last, float m_a, float m_b,
+                                            bool last_piece) {
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x - kSoftmaxWarp0 * 32;
   const int q4 = lane & 3;
   const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
   const int gqa = c.gqa;
@@ -654,8 +668,21 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
   const float l_a = __uint_as_float(sums[0]), l_b = __uint_as_float(sums[2]);
   if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1900 + G_last);
   const bool whole = (r.lo == 0 && r.hi == r.nb);
-  const long long slot = whole ? 0 : piece_slot(c.w, worker_of(r.ustart, c.total, c.workers));
   const int first_row = c.ps.gfirst[r.g];
+  long long w0 = 0, w1 = 0, slot = 0, oslot = 0, unit = 0;
+  bool direct = false;
+  if (!whole) {
+    w0 = worker_of(r.ustart, c.total, c.workers);
+    w1 = worker_of(r.ustart + r.nb - 1, c.total, c.workers);
+    slot = piece_slot(c.w, w0);
+    oslot = piece_slot(c.w == w0 ? w1 : w0, w0);
+    unit = (long long)r.g * c.hk + r.h;
+    if (last_piece && w1 - w0 == 1) {
+      if (tid == 0) sh->merge_mode = ld_acquire_gpu(p.counters + unit) == 1;
+      named_bar_sync(2, kSoftmaxThreads);
+      direct = sh->merge_mode != 0;
+    }
+  }
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     uint32_t o[32];
@@ -669,29 +696,73 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
     for (int x = 0; x < 2; ++x) {
       const int j = x == 0 ? r.ja : r.jb;
       if (j >= 0) {
-        const float inv = 1.f / (x == 0 ? l_a : l_b);
+        const float l = x == 0 ? l_a : l_b, m = x == 0 ? m_a : m_b;
+        const float inv = 1.f / l;
         const int row = first_row + j / gqa;
         const int head = r.h * gqa + j % gqa;
+        __half* out = p.o + ((long long)row * p.num_q_heads + head) * kHeadDim + half * 64;
         if (whole) {
-          __half* dst = p.o + ((long long)row * p.num_q_heads + head) * kHeadDim + half * 64;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<uint32_t*>(dst + 8 * i + 2 * q4) =
+            *reinterpret_cast<uint32_t*>(out + 8 * i + 2 * q4) =
                 pack_half2(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv);
-        } else {
+        } else if (!direct) {
           float* dst = p.part_o + (slot * p.nq + j) * kHeadDim + half * 64;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
             __stcg(reinterpret_cast<float2*>(dst + 8 * i + 2 * q4),
                    make_float2(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv));
-          if (half == 0 && q4 == 0) {
-            const float l = x == 0 ? l_a : l_b;
-            const float m = x == 0 ? m_a : m_b;
-            __stcg(p.part_lse + slot * p.nq + j, l > 0.f ? m + __log2f(l) : neg_inf());
+          if (half == 0 && q4 == 0) __stcg(p.part_lse + slot * p.nq + j, l > 0.f ? m + __log2f(l) : neg_inf());
+        } else {
+          // Log-sum-exp of this piece (in registers) and the other piece's partial.
+          const float* src = p.part_o + (oslot * p.nq + j) * kHeadDim + half * 64;
+          float2 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __ldcg(reinterpret_cast<const float2*>(src + 8 * i + 2 * q4));
+          const float le_o = __ldcg(p.part_lse + oslot * p.nq + j);
+          const float le_s = l > 0.f ? m + __log2f(l) : neg_inf();
+          // A piece with no unmasked token (lse -inf) carries no weight, and its
+          // values (0/0) are not read; both empty gives NaN, as in the reference.
+          const bool has_s = le_s != neg_inf(), has_o = le_o != neg_inf();
+          const float mx = fmaxf(le_s, le_o);
+          const float ws = has_s ? fast_exp2(le_s - mx) : 0.f;
+          const float wo = has_o ? fast_exp2(le_o - mx) : 0.f;
+          const float rden = 1.f / (ws + wo);
+          const float fs = has_s ? ws * inv * rden : 0.f, fo = has_o ? wo * rden : 0.f;
+          const float nan = __int_as_float(0x7fc00000);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float ox = has_s ? __uint_as_float(o[4 * i]) * fs : 0.f, oy = has_s ? __uint_as_float(o[4 * i + 1]) * fs : 0.f;
+            if (has_o) {
+              ox += v[i].x * fo;
+              oy += v[i].y * fo;
+            }
+            if (!has_s && !has_o) ox = oy = nan;
+            *reinterpret_cast<uint32_t*>(out + 8 * i + 2 * q4) = pack_half2(ox, oy);
           }
         }
       }
       swap_rows_n<8>(o);  // row b's values into row a's registers
+    }
+  }
+  if (!whole) {
+    if (direct) {
+      if (tid == 0) p.counters[unit] = 0;  // the unit is complete: ready for the next call
+    } else if (!last_piece) {
+      warp_arrive(&sh->part_ready);  // the K warp counts it in
+    } else {
+      named_bar_sync(2, kSoftmaxThreads);  // every partial store precedes thread 0's fence
+      if (tid == 0) {
+        __threadfence();
+        const int last = atomicAdd(p.counters + unit, 1) == (int)(w1 - w0);
+        if (last) p.counters[unit] = 0;
+        sh->merge_mode = last;
+      }
+      named_bar_sync(2, kSoftmaxThreads);
+      if (sh->merge_mode) {
+        __threadfence();
+        merge_unit_threads(p, first_row, c.ps.gfirst[r.g + 1] - first_row, r.h, gqa, w0, w1, tid, kSoftmaxThreads);
+      }
     }
   }
   if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1800 + G_last);
@@ -879,7 +950,7 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
       if (lane == 0 && G < 100) NEB_TRACE_POINT(c, 608 + 4 * G + (warp - kSoftmaxWarp0));
     }
     if (!ok) break;
-    if (!piece_epilogue(c, cr, G - 1, m_a, m_b)) break;
+    if (!piece_epilogue(c, cr, G - 1, m_a, m_b, !have_next)) break;
     have = have_next;
     cr = nr;
   }
@@ -943,6 +1014,8 @@ __global__ void __launch_bounds__(kVThreads, 1)
       mbar_init(&sh->q_empty[i], 1);
     }
     mbar_init(&sh->o_empty, 4);
+    mbar_init(&sh->part_ready, 4);
+    sh->first_last = 0;
     mbar_init(&sh->s_final, 1);
     mbar_init(&sh->pv_final, 1);
     sh->abort_flag = 0;
@@ -959,9 +1032,11 @@ __global__ void __launch_bounds__(kVThreads, 1)
   if (threadIdx.x == 0) NEB_TRACE_POINT(c, 2);
 
   if (warp == kKWarp) {
-    producer(c, &tmap_k, sh->k_full, sh->k_empty, kKOff, 1);
+    FirstSplit first;
+    first.init(c);
+    producer(c, &tmap_k, sh->k_full, sh->k_empty, kKOff, 1, &first);
   } else if (warp == kVWarp) {
-    producer(c, &tmap_v, sh->v_full, sh->v_empty, kVOff, 0);
+    producer(c, &tmap_v, sh->v_full, sh->v_empty, kVOff, 0, nullptr);
   } else if (warp == kSWarp) {
     if (lane == 0) s_issuer(c, &tmap_q);
   } else if (warp == kPVWarp) {
@@ -974,7 +1049,7 @@ __global__ void __launch_bounds__(kVThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == kSWarp) tmem_dealloc(c.tmem, kTmemCols);
-  if (!aborted(sh)) finish_split_units(c, scratch);
+  if (!aborted(sh) && sh->first_last) finish_first_unit(c);
   if (threadIdx.x == 0) NEB_TRACE_POINT(c, 4);
 }
 
