@@ -67,6 +67,15 @@ def _dist():
     return world, rank, local
 
 
+def max_over_ranks(ms: float, device, world: int) -> float:
+    """The job's time: the slowest rank's (each rank times its own stream)."""
+    if world <= 1:
+        return ms
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
 def _peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -205,11 +214,7 @@ def run_ours(args):
         torch.cuda.synchronize()
         barrier()
     ms = e0.elapsed_time(e1)
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = max_over_ranks(ms, dev, world)
     per_step = step_bytes(b, layers)
     total_bytes = per_step * args.steps * world
     value = total_bytes / (ms_max * 1e-3) / 1e12
@@ -254,11 +259,7 @@ def run_ours(args):
     f1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    ems = f0.elapsed_time(f1)
-    if world > 1:
-        t = torch.tensor([ems], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ems = float(t.item())
+    ems = max_over_ranks(f0.elapsed_time(f1), dev, world)
     e2e_value = per_step * e2e_steps * world / (ems * 1e-3) / 1e12
     h2d = q_host.numel() * 2 + lens_host.numel() * 4 + ids_host.numel() * 4 + bt_host.numel() * 4
     d2h = o_host.numel() * 2
