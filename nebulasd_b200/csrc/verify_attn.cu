@@ -80,6 +80,7 @@ constexpr uint32_t kSBuf = 64;                            // S tile b at columns
 constexpr uint32_t kOCol = 256;                           // O: 128 columns
 constexpr uint32_t kSumCol = 384;                         // P x ones: every column holds the row sum
 constexpr long long kWaitLimit = 4000000000LL;
+constexpr int kMaxDirectOthers = 3;                      // direct merge: at most 3 other pieces
 static_assert(kStageCols <= (int)kSBuf && kStageR % 2 == 0 && kSBufs * kSBuf <= kOCol, "S tiles fit TMEM");
 
 // Shared memory map (offsets from a 1024-byte aligned base).
@@ -388,6 +389,7 @@ struct FirstSplit {
       c.sh->first_last = 1;
     }
     pending = false;
+    NEB_TRACE_POINT(c, 1997);
   }
 };
 
@@ -659,6 +661,24 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
   const int q4 = lane & 3;
   const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
   const int gqa = c.gqa;
+  const bool whole = (r.lo == 0 && r.hi == r.nb);
+  const int first_row = c.ps.gfirst[r.g];
+  long long w0 = 0, w1 = 0, slot = 0, unit = 0;
+  bool direct = false;
+  if (!whole) {
+    w0 = worker_of(r.ustart, c.total, c.workers);
+    w1 = worker_of(r.ustart + r.nb - 1, c.total, c.workers);
+    slot = piece_slot(c.w, w0);
+    unit = (long long)r.g * c.hk + r.h;
+    // The counter is read while the last P V still runs.
+    if (last_piece && w1 - w0 <= kMaxDirectOthers) {
+      if (tid == 0) sh->merge_mode = ld_acquire_gpu(p.counters + unit) == (int)(w1 - w0);
+      named_bar_sync(2, kSoftmaxThreads);
+      direct = sh->merge_mode != 0;
+      if (tid == 0) NEB_TRACE_POINT(c, 1990);
+      if (tid == 0 && c.trace) c.trace[1995] = direct ? 1 : 2;
+    }
+  }
   if (!wait_or_abort(sh, p, &sh->pv_done[G_last & 1], (uint32_t)((G_last >> 1) & 1))) return false;
   if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1508 + G_last);
   tc_fence_after();
@@ -667,22 +687,6 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
   tmem_wait_ld();
   const float l_a = __uint_as_float(sums[0]), l_b = __uint_as_float(sums[2]);
   if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1900 + G_last);
-  const bool whole = (r.lo == 0 && r.hi == r.nb);
-  const int first_row = c.ps.gfirst[r.g];
-  long long w0 = 0, w1 = 0, slot = 0, oslot = 0, unit = 0;
-  bool direct = false;
-  if (!whole) {
-    w0 = worker_of(r.ustart, c.total, c.workers);
-    w1 = worker_of(r.ustart + r.nb - 1, c.total, c.workers);
-    slot = piece_slot(c.w, w0);
-    oslot = piece_slot(c.w == w0 ? w1 : w0, w0);
-    unit = (long long)r.g * c.hk + r.h;
-    if (last_piece && w1 - w0 == 1) {
-      if (tid == 0) sh->merge_mode = ld_acquire_gpu(p.counters + unit) == 1;
-      named_bar_sync(2, kSoftmaxThreads);
-      direct = sh->merge_mode != 0;
-    }
-  }
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     uint32_t o[32];
@@ -714,37 +718,62 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
                    make_float2(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv));
           if (half == 0 && q4 == 0) __stcg(p.part_lse + slot * p.nq + j, l > 0.f ? m + __log2f(l) : neg_inf());
         } else {
-          // Log-sum-exp of this piece (in registers) and the other piece's partial.
-          const float* src = p.part_o + (oslot * p.nq + j) * kHeadDim + half * 64;
-          float2 v[8];
+          // Log-sum-exp of the unit's pieces in worker order, this one from
+          // registers and the others from their partials, with the arithmetic
+          // of merge_unit_threads (one round of at most four slots), so that
+          // the result does not depend on which path merged the unit.  A
+          // piece with no unmasked token (lse -inf) carries no weight; all
+          // empty gives 0/0 = NaN, as in the reference.
+          constexpr int kN = kMaxDirectOthers + 1;
+          float le[kN];
+          float2 v[kN][8];
+          const int self = (int)(c.w - w0);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = __ldcg(reinterpret_cast<const float2*>(src + 8 * i + 2 * q4));
-          const float le_o = __ldcg(p.part_lse + oslot * p.nq + j);
-          const float le_s = l > 0.f ? m + __log2f(l) : neg_inf();
-          // A piece with no unmasked token (lse -inf) carries no weight, and its
-          // values (0/0) are not read; both empty gives NaN, as in the reference.
-          const bool has_s = le_s != neg_inf(), has_o = le_o != neg_inf();
-          const float mx = fmaxf(le_s, le_o);
-          const float ws = has_s ? fast_exp2(le_s - mx) : 0.f;
-          const float wo = has_o ? fast_exp2(le_o - mx) : 0.f;
-          const float rden = 1.f / (ws + wo);
-          const float fs = has_s ? ws * inv * rden : 0.f, fo = has_o ? wo * rden : 0.f;
-          const float nan = __int_as_float(0x7fc00000);
+          for (int k = 0; k < kN; ++k) {
+            le[k] = neg_inf();
+            if (k == self) {
+              le[k] = l > 0.f ? m + __log2f(l) : neg_inf();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float ox = has_s ? __uint_as_float(o[4 * i]) * fs : 0.f, oy = has_s ? __uint_as_float(o[4 * i + 1]) * fs : 0.f;
-            if (has_o) {
-              ox += v[i].x * fo;
-              oy += v[i].y * fo;
+              for (int i = 0; i < 8; ++i)
+                v[k][i] = make_float2(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv);
+            } else if (w0 + k <= w1) {
+              const long long sk = piece_slot(w0 + k, w0);
+              le[k] = __ldcg(p.part_lse + sk * p.nq + j);
+              const float* src = p.part_o + (sk * p.nq + j) * kHeadDim + half * 64;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[k][i] = __ldcg(reinterpret_cast<const float2*>(src + 8 * i + 2 * q4));
             }
-            if (!has_s && !has_o) ox = oy = nan;
-            *reinterpret_cast<uint32_t*>(out + 8 * i + 2 * q4) = pack_half2(ox, oy);
           }
+          float mx = neg_inf();
+#pragma unroll
+          for (int k = 0; k < kN; ++k) mx = fmaxf(mx, le[k]);
+          float den = 0.f;
+          float2 acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
+          if (mx != neg_inf()) {
+#pragma unroll
+            for (int k = 0; k < kN; ++k) {
+              if (le[k] == neg_inf()) continue;
+              const float wt = fast_exp2(le[k] - mx);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                acc[i].x += wt * v[k][i].x;
+                acc[i].y += wt * v[k][i].y;
+              }
+              den += wt;
+            }
+          }
+          const float rden = 1.f / den;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint32_t*>(out + 8 * i + 2 * q4) = pack_half2(acc[i].x * rden, acc[i].y * rden);
         }
       }
       swap_rows_n<8>(o);  // row b's values into row a's registers
     }
   }
+  if (tid == 0 && last_piece) NEB_TRACE_POINT(c, 1991);
   if (!whole) {
     if (direct) {
       if (tid == 0) p.counters[unit] = 0;  // the unit is complete: ready for the next call
@@ -757,6 +786,8 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
         const int last = atomicAdd(p.counters + unit, 1) == (int)(w1 - w0);
         if (last) p.counters[unit] = 0;
         sh->merge_mode = last;
+        NEB_TRACE_POINT(c, 1992);
+        if (c.trace) c.trace[1996] = last ? 3 : 4;
       }
       named_bar_sync(2, kSoftmaxThreads);
       if (sh->merge_mode) {

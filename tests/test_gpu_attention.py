@@ -156,6 +156,13 @@ def test_target_verify_full_size_property(kernel, cuda):
                         kernel=_kernel_id(kernel))
     torch.cuda.synchronize()
     assert torch.isfinite(o).all()
+    # Units cut across CTAs are merged by whichever piece ends last, by one of
+    # two paths; both give the same bits, so a second call reproduces the first.
+    o2 = torch.empty_like(o)
+    paged_attention_raw(b.q, b.k_cache, b.v_cache, b.block_table, b.seq_lens, b.seq_ids, 0, 128 ** -0.5, o2,
+                        kernel=_kernel_id(kernel))
+    torch.cuda.synchronize()
+    assert torch.equal(o, o2)
     for req in (0, 7, 15):
         rows = [i for i, s in enumerate(b.seq_ids_list) if s == req]
         nb = (max(b.seq_lens_list[i] for i in rows) + 15) // 16
