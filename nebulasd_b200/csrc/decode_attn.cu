@@ -184,7 +184,7 @@ template <int GQA>
 __global__ void __launch_bounds__(kDecodeThreads, (GQA <= 2 ? 4 : 2)) decode_attn_kernel(AttnParams p) {
   extern __shared__ int smem[];
   __shared__ int scratch[32];
-  PlanSmem ps{smem, smem + (p.num_rows + 1), smem + 2 * (p.num_rows + 1)};
+  PlanSmem ps{smem, smem + (p.num_rows + 1), smem + 2 * (p.num_rows + 1), nullptr};
   build_plan(ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, 1);
   const int ng = ps.misc[0];
   const int hk = p.num_kv_heads;

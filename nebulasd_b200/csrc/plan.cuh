@@ -31,10 +31,11 @@ struct PlanSmem {
   int* gfirst;   // [R + 1]  first row of group g; gfirst[NG] = R
   int* gprefix;  // [R + 1]  exclusive prefix of tiles per head; gprefix[NG] = total
   int* misc;     // [8]      misc[0] = NG
+  int* gsid;     // [R + 1]  seq id of group g (optional: null when not kept)
 };
 
-__host__ __device__ inline size_t plan_smem_bytes(int num_rows) {
-  return (size_t)(2 * (num_rows + 1) + 8) * sizeof(int);
+__host__ __device__ inline size_t plan_smem_bytes(int num_rows, bool with_sid = false) {
+  return (size_t)((with_sid ? 3 : 2) * (num_rows + 1) + 8) * sizeof(int);
 }
 
 // Block-wide inclusive scan (sum or max) of one value per thread.  `scratch`
@@ -83,13 +84,17 @@ static __device__ __noinline__ void build_plan(PlanSmem ps, int* scratch, const 
       sid = seq_ids[r];
       prev = r > 0 ? seq_ids[r - 1] : 0;
       seq_start = (r == 0) || (sid != prev);
+      ps.gprefix[r] = seq_lens[r];  // row lengths, read back by pass 2 (one coalesced load)
     }
     int run_start = block_inclusive_scan<true>(seq_start ? r : 0, scratch);
     run_start = max(run_start, carry_run);
     bool gstart = false;
     if (r < num_rows) gstart = seq_start || ((r - run_start) % max_group_rows == 0);
     int gidx = block_inclusive_scan<false>(gstart ? 1 : 0, scratch) + carry_groups - 1;
-    if (r < num_rows && gstart) ps.gfirst[gidx] = r;
+    if (r < num_rows && gstart) {
+      ps.gfirst[gidx] = r;
+      if (ps.gsid) ps.gsid[gidx] = sid;
+    }
     // carries from the last thread of the chunk
     if (threadIdx.x == blockDim.x - 1) {
       scratch[0] = run_start;
@@ -112,8 +117,11 @@ static __device__ __noinline__ void build_plan(PlanSmem ps, int* scratch, const 
     const int g = base + threadIdx.x;
     int nb = 0;
     if (g < ng) {
+      // Lengths of the group's rows (>= g), kept in gprefix by pass 1: every
+      // thread reads them before the scan's first barrier and writes only
+      // gprefix[g] (< the next chunk's rows) after it.
       int mx = 0;
-      for (int r = ps.gfirst[g]; r < ps.gfirst[g + 1]; ++r) mx = max(mx, (int)seq_lens[r]);
+      for (int r = ps.gfirst[g]; r < ps.gfirst[g + 1]; ++r) mx = max(mx, ps.gprefix[r]);
       nb = (mx + 15) >> 4;
     }
     int incl = block_inclusive_scan<false>(nb, scratch);

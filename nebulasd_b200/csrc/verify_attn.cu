@@ -101,7 +101,7 @@ static_assert(kHalf % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 
 // Largest row count whose plan arrays still fit next to the fixed buffers
 // (227 KiB per CTA, less the alignment pad and 256 bytes of static shared memory).
-constexpr int kVerifyMaxRows = ((232448 - 1024 - 256 - (int)kPlanOff) / 4 - 8) / 2 - 1;
+constexpr int kVerifyMaxRows = ((232448 - 1024 - 256 - (int)kPlanOff) / 4 - 8) / 3 - 1;
 static_assert(kVerifyMaxRows >= 1024, "room for the plan of a large verify batch");
 
 struct VerifyShared {
@@ -129,7 +129,7 @@ struct VerifyShared {
 static_assert(sizeof(VerifyShared) <= 1024, "barrier block fits its slot");
 
 __host__ __device__ inline size_t verify_smem_bytes(int num_rows) {
-  return 1024 + kPlanOff + plan_smem_bytes(num_rows);
+  return 1024 + kPlanOff + plan_smem_bytes(num_rows, true);
 }
 
 struct VerifyArgs {
@@ -311,7 +311,7 @@ struct TileFeed {
     const int rel = (int)(t - (long long)hk * ps->gprefix[g]);  // < hk * nb
     q.kv_head = rel / nb;
     q.tile = rel - q.kv_head * nb;
-    q.sid = __ldg(p->seq_ids + ps->gfirst[g]);
+    q.sid = ps->gsid[g];
     q.in_range = true;
     return q;
   }
@@ -1008,7 +1008,8 @@ __global__ void __launch_bounds__(kVThreads, 1)
 #endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) NEB_TRACE_POINT(c, 0);
-  c.ps = PlanSmem{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1)};
+  c.ps = PlanSmem{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1),
+                  plan_mem + 2 * (p.num_rows + 1) + 8};
   build_plan(c.ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, p.max_group_rows);
   c.ng = c.ps.misc[0];
   if (threadIdx.x == 0) NEB_TRACE_POINT(c, 1);
