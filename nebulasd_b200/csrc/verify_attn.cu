@@ -407,6 +407,9 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
   VerifyShared* sh = c.sh;
   const int lane = threadIdx.x & 31;
   if (lane == 0) tma_prefetch_desc(tmap);
+  // K and V tiles are read once: let them leave L2 first, so that the kernel's
+  // code, the plan inputs, q and the merge partials stay cached.
+  const uint64_t kv_policy = l2_evict_first_policy();
   TileFeed feed;
   feed.init(&p, &c.ps, c.ng, c.oob_row, c.t_begin, c.t_end);
   PieceCursor cur;
@@ -439,8 +442,8 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
           mbar_arrive_expect_tx(&full[slot], (uint32_t)nblk * 2u * 2048u);
 #pragma unroll 1
           for (int b = 0; b < nblk; ++b) {
-            tma_load_2d(dst + b * 2048, tmap, &full[slot], 0, rows[b]);
-            tma_load_2d(dst + kHalf + b * 2048, tmap, &full[slot], 64, rows[b]);
+            tma_load_2d_hint(dst + b * 2048, tmap, &full[slot], 0, rows[b], kv_policy);
+            tma_load_2d_hint(dst + kHalf + b * 2048, tmap, &full[slot], 64, rows[b], kv_policy);
           }
         }
       }
