@@ -145,6 +145,48 @@ __device__ __forceinline__ int find_group(const int* gprefix, int ng, long long 
   return lo;
 }
 
+// Cost-weighted split.  Each unit (group, kv head) counts `pc` extra virtual
+// tiles ahead of its own tiles: the fixed cost of starting a piece (its
+// epilogue, the pipeline refill).  Unit u = hk*g + h starts at virtual
+// position hk*(gprefix[g] + pc*g) + h*(nb_g + pc), and its tile t sits at
+// t + pc*(u + 1); V = T + pc*hk*ng.  Workers split [0, V) evenly; a worker's
+// tiles are the ones whose virtual positions fall in its share, a contiguous
+// range of tiles as with pc = 0 (which reproduces the plain tile split).
+struct CostSplit {
+  const int* gprefix;
+  int ng, hk, pc;
+  long long vtotal, workers;
+
+  __device__ __forceinline__ long long vbase(int g) const {
+    return (long long)hk * ((long long)gprefix[g] + (long long)pc * g);
+  }
+  // Virtual position of tile t (t < T).
+  __device__ __forceinline__ long long vpos(long long t) const {
+    const int g = find_group(gprefix, ng, t, hk);
+    const int nb = gprefix[g + 1] - gprefix[g];
+    const int h = (int)((t - (long long)hk * gprefix[g]) / nb);
+    return t + (long long)pc * ((long long)g * hk + h + 1);
+  }
+  // First tile whose virtual position is >= v (T when none).
+  __device__ __forceinline__ long long tile_at(long long v) const {
+    if (v >= vtotal) return (long long)hk * gprefix[ng];
+    int lo = 0, hi = ng;  // largest g with vbase(g) <= v
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (vbase(mid) <= v) lo = mid; else hi = mid;
+    }
+    const int nb = gprefix[lo + 1] - gprefix[lo];
+    const long long off = v - vbase(lo);
+    const long long h = off / (nb + pc);
+    const long long in_unit = off - h * (nb + pc);
+    return (long long)hk * gprefix[lo] + h * nb + (in_unit > pc ? in_unit - pc : 0);
+  }
+  __device__ __forceinline__ long long begin(long long w) const { return tile_at((w * vtotal) / workers); }
+  __device__ __forceinline__ long long worker_of_tile(long long t) const {
+    return ((vpos(t) + 1) * workers - 1) / vtotal;
+  }
+};
+
 // Slot of the partial written by worker w for a unit whose first worker is w0.
 __host__ __device__ __forceinline__ long long piece_slot(long long w, long long w0) {
   return w == w0 ? 2 * w + 1 : 2 * w;

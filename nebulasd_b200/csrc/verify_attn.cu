@@ -81,6 +81,7 @@ constexpr uint32_t kOCol = 256;                           // O: 128 columns
 constexpr uint32_t kSumCol = 384;                         // P x ones: every column holds the row sum
 constexpr long long kWaitLimit = 4000000000LL;
 constexpr int kMaxDirectOthers = 3;                      // direct merge: at most 3 other pieces
+constexpr int kPieceCost = 8;                             // a piece's fixed cost, in tiles (plan.cuh CostSplit)
 static_assert(kStageCols <= (int)kSBuf && kStageR % 2 == 0 && kSBufs * kSBuf <= kOCol, "S tiles fit TMEM");
 
 // Shared memory map (offsets from a 1024-byte aligned base).
@@ -145,6 +146,7 @@ struct Ctx {
   PlanSmem ps;
   int ng, hk, gqa, oob_row;
   long long total, workers, w, t_begin, t_end;
+  CostSplit split;  // which worker owns which tiles
   uint32_t tmem;
   unsigned long long* trace;  // timeline buffer row of this CTA (builds with NEB_TRACE only)
 };
@@ -375,8 +377,8 @@ struct FirstSplit {
     if ((lo == 0 && hi == nb) || c.t_begin + (hi - lo) >= c.t_end) return;
     pending = true;
     unit = (long long)g * c.hk + h;
-    w0 = worker_of(ustart, c.total, c.workers);
-    w1 = worker_of(ustart + nb - 1, c.total, c.workers);
+    w0 = c.split.worker_of_tile(ustart);
+    w1 = c.split.worker_of_tile(ustart + nb - 1);
   }
   // Lane-0 work once the softmax has arrived: publish the partial and count it.
   __device__ __noinline__ void count(const Ctx& c) {
@@ -669,8 +671,8 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
   long long w0 = 0, w1 = 0, slot = 0, unit = 0;
   bool direct = false;
   if (!whole) {
-    w0 = worker_of(r.ustart, c.total, c.workers);
-    w1 = worker_of(r.ustart + r.nb - 1, c.total, c.workers);
+    w0 = c.split.worker_of_tile(r.ustart);
+    w1 = c.split.worker_of_tile(r.ustart + r.nb - 1);
     slot = piece_slot(c.w, w0);
     unit = (long long)r.g * c.hk + r.h;
     // The counter is read while the last P V still runs.
@@ -1025,10 +1027,16 @@ __global__ void __launch_bounds__(kVThreads, 1)
   if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4)
     write_nan_rows(p, c.ps, c.ng, c.w * 4 + (warp - kSoftmaxWarp0), launched * 4);
   if (c.total == 0) return;
-  c.workers = launched < c.total ? launched : c.total;
+  c.split.gprefix = c.ps.gprefix;
+  c.split.ng = c.ng;
+  c.split.hk = c.hk;
+  c.split.pc = kPieceCost;
+  c.split.vtotal = c.total + (long long)kPieceCost * c.hk * c.ng;
+  c.workers = launched < c.split.vtotal ? launched : c.split.vtotal;
+  c.split.workers = c.workers;
   if (c.w >= c.workers) return;
-  c.t_begin = range_begin(c.w, c.total, c.workers);
-  c.t_end = range_begin(c.w + 1, c.total, c.workers);
+  c.t_begin = c.split.begin(c.w);
+  c.t_end = c.split.begin(c.w + 1);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRing; ++i) {

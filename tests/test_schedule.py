@@ -23,8 +23,8 @@ def test_groups_follow_seq_runs_and_cap():
     assert S.groups([1, 1], [0, 0], 4) == [(0, 2, 0)]
 
 
-def _check_partition(ids, lens, hk, workers, mg):
-    ps = S.pieces(ids, lens, hk, workers, mg)
+def _check_partition(ids, lens, hk, workers, mg, pc=0):
+    ps = S.pieces(ids, lens, hk, workers, mg, pc)
     gs = S.groups(ids, lens, mg)
     covered = {}
     slots = set()
@@ -45,14 +45,25 @@ def _check_partition(ids, lens, hk, workers, mg):
         w0, w1 = pieces[0].w0, pieces[0].w1
         assert [p.worker for p in pieces] == list(range(w0, w1 + 1))
         assert sorted(p.slot for p in pieces) == sorted(S.piece_slot(w, w0) for w in range(w0, w1 + 1))
-    # balance: every worker gets floor or ceil of T/W tiles
     load = {}
+    starts = {}
     for p in ps:
         load[p.worker] = load.get(p.worker, 0) + p.tile_hi - p.tile_lo
+        starts[p.worker] = starts.get(p.worker, 0) + (p.tile_lo == 0)
     total = sum(load.values())
-    workers = min(workers, total) if total else workers
-    for w in range(workers):
-        assert load.get(w, 0) in (total // workers, -(-total // workers))
+    if pc == 0:
+        # balance: every worker gets floor or ceil of T/W tiles
+        workers = min(workers, total) if total else workers
+        for w in range(workers):
+            assert load.get(w, 0) in (total // workers, -(-total // workers))
+    elif all(nb > 0 for _, _, nb in gs):
+        # balance of tiles + pc per unit started, within one piece's cost
+        # (an empty unit carries cost but no piece, so batches with one are skipped)
+        vtotal = total + pc * hk * len(gs)
+        workers = min(workers, vtotal)
+        for w in range(workers):
+            cost = load.get(w, 0) + pc * starts.get(w, 0)
+            assert abs(cost - vtotal / workers) <= pc + 1
 
 
 @pytest.mark.parametrize("seed", range(40))
@@ -78,3 +89,34 @@ def test_partition_exhaustive_small():
         for workers in (1, 2, 5, 9):
             _check_partition([0, 1, 2], list(lens), 2, workers, 1)
             _check_partition([0, 0, 0], list(lens), 2, workers, 2)
+
+
+@pytest.mark.parametrize("seed", range(40))
+@pytest.mark.parametrize("pc", [1, 5, 12])
+def test_cost_split_partition(seed, pc):
+    rng = random.Random(1000 + seed)
+    nreq = rng.randint(1, 12)
+    ids, lens = [], []
+    for r in range(nreq):
+        depth = rng.randint(0, 9)
+        base = rng.choice([0, 1, 15, 16, 17, rng.randint(1, 700)])
+        sid = rng.randint(0, 5) if rng.random() < 0.3 else r
+        for j in range(depth + 1):
+            ids.append(sid)
+            lens.append(base + j)
+    _check_partition(ids, lens, rng.choice([1, 2, 8]), rng.choice([1, 2, 3, 7, 148, 600]), rng.choice([1, 4, 16]), pc)
+
+
+def test_cost_split_inverse_and_zero_cost_identity():
+    prefix = [0, 3, 3, 10, 11]   # one empty group
+    for hk in (1, 2, 8):
+        for pc in (0, 1, 7):
+            for workers in (1, 3, 10, 50):
+                sp = S.CostSplit(prefix, hk, pc, workers)
+                bounds = [sp.begin(w) for w in range(sp.workers + 1)]
+                assert bounds[0] == 0 and bounds[-1] == sp.total and bounds == sorted(bounds)
+                for t in range(sp.total):
+                    w = sp.worker_of_tile(t)
+                    assert bounds[w] <= t < bounds[w + 1]
+                if pc == 0:
+                    assert bounds == [S.range_begin(w, sp.total, sp.workers) for w in range(sp.workers + 1)]
