@@ -805,6 +805,75 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
   return true;
 }
 
+// Scores of one stage in place (sr holds the fp32 bits of a 16x256b TMEM
+// load): scaled into the exp2 domain and masked to -inf, and the running max
+// of each of the kRows rows this thread holds over its quad.  Element (r, e)
+// of row x is sr[4r + 2x + e], at token 8r + 2*q4 + e of the stage; it is
+// valid iff 8r + e < lim[x] and its block's flag is set.  Both rows go through
+// one pass so that their instruction chains interleave.
+template <int kRows>
+__device__ __forceinline__ void mask_max_rows(uint32_t* sr, const int* lim, int blk_ok, bool blocks_ok, float sc,
+                                              float* mx) {
+#pragma unroll
+  for (int x = 0; x < kRows; ++x)
+#pragma unroll
+    for (int r = 0; r < kStageR; ++r)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float v = 8 * r + e < lim[x] ? __uint_as_float(sr[4 * r + 2 * x + e]) * sc : neg_inf();
+        sr[4 * r + 2 * x + e] = __float_as_uint(v);
+      }
+  if (!blocks_ok) {
+#pragma unroll
+    for (int r = 0; r < kStageR; ++r)
+      if (!((blk_ok >> (r >> 1)) & 1))
+#pragma unroll
+        for (int x = 0; x < kRows; ++x) sr[4 * r + 2 * x] = sr[4 * r + 2 * x + 1] = __float_as_uint(neg_inf());
+  }
+#pragma unroll
+  for (int x = 0; x < kRows; ++x) {
+    float t[kStageR];
+#pragma unroll
+    for (int r = 0; r < kStageR; ++r)
+      t[r] = fmaxf(__uint_as_float(sr[4 * r + 2 * x]), __uint_as_float(sr[4 * r + 2 * x + 1]));
+#pragma unroll
+    for (int w2 = kStageR / 2; w2 >= 1; w2 /= 2)
+#pragma unroll
+      for (int r = 0; r < w2; ++r) t[r] = fmaxf(t[r], t[r + w2]);
+    mx[x] = t[0];
+  }
+#pragma unroll
+  for (int x = 0; x < kRows; ++x) mx[x] = fmaxf(mx[x], __shfl_xor_sync(0xffffffffu, mx[x], 1));
+#pragma unroll
+  for (int x = 0; x < kRows; ++x) mx[x] = fmaxf(mx[x], __shfl_xor_sync(0xffffffffu, mx[x], 2));
+}
+
+// P = 2^(s - m) as fp16 pairs (the MMA operand) into the swizzled P tile for
+// the kRows rows of this thread (MMA rows mrow[x]); rows with nothing
+// unmasked yet (m = -inf) get zeros.
+template <int kRows>
+__device__ __forceinline__ void store_p_rows(const uint32_t* sr, const float* m, const int* mrow, uint8_t* pbuf,
+                                             int q4) {
+  uint32_t pv[kRows][kStageR];
+#pragma unroll
+  for (int x = 0; x < kRows; ++x)
+#pragma unroll
+    for (int r = 0; r < kStageR; ++r)
+      pv[x][r] = pack_half2(__uint_as_float(sr[4 * r + 2 * x]) - m[x], __uint_as_float(sr[4 * r + 2 * x + 1]) - m[x]);
+#pragma unroll
+  for (int x = 0; x < kRows; ++x)
+#pragma unroll
+    for (int r = 0; r < kStageR; ++r) pv[x][r] = m[x] != neg_inf() ? ex2_f16x2(pv[x][r]) : 0u;
+#pragma unroll
+  for (int x = 0; x < kRows; ++x) {
+    uint8_t* prow = pbuf + mrow[x] * 128 + q4 * 4;
+    const int sw = mrow[x] & 7;
+#pragma unroll
+    for (int r = 0; r < kStageR; ++r)
+      *reinterpret_cast<uint32_t*>(prow + (r >> 3) * kPAtom + (((r & 7) ^ sw) << 4)) = pv[x][r];
+  }
+}
+
 __device__ __noinline__ void softmax_role(const Ctx& c) {
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
@@ -891,43 +960,16 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
       const int t0 = cr.lo + s * kStageBlocks;
       const int nblk = min(kStageBlocks, cr.hi - t0);
       const int tok0 = t0 * kBlockTokens;
-      // Scores in place (sr holds fp32 bits): scaled into the exp2 domain and
-      // masked to -inf.  Element (r, e) of row a is sr[4r + e], of row b
-      // sr[4r + 2 + e], at token tok0 + 8r + 2*q4 + e.  One copy of the code
-      // serves both rows: row b is swapped into row a's registers and back.
-      float mxa = neg_inf(), mxb = neg_inf();
+      float mxs[2];
       const bool blocks_ok = __all_sync(0xffffffffu, blk_ok == (1 << nblk) - 1);
-#pragma unroll 1
-      for (int x = 0; x < (has_b ? 2 : 1); ++x) {
-        const int lim = (x == 0 ? cr.len_a : cr.len_b) - tok0 - 2 * q4;  // (r, e) valid iff 8r + e < lim
-#pragma unroll
-        for (int r = 0; r < kStageR; ++r)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float v = 8 * r + e < lim ? __uint_as_float(sr[4 * r + e]) * sc : neg_inf();
-            sr[4 * r + e] = __float_as_uint(v);
-          }
-        if (!blocks_ok) {
-#pragma unroll
-          for (int r = 0; r < kStageR; ++r)
-            if (!((blk_ok >> (r >> 1)) & 1)) sr[4 * r] = sr[4 * r + 1] = __float_as_uint(neg_inf());
-        }
-        float t[kStageR];
-#pragma unroll
-        for (int r = 0; r < kStageR; ++r) t[r] = fmaxf(__uint_as_float(sr[4 * r]), __uint_as_float(sr[4 * r + 1]));
-#pragma unroll
-        for (int w2 = kStageR / 2; w2 >= 1; w2 /= 2)
-#pragma unroll
-          for (int r = 0; r < w2; ++r) t[r] = fmaxf(t[r], t[r + w2]);
-        if (x == 0) mxa = t[0]; else mxb = t[0];
-        if (has_b) swap_rows_n<kStageR>(sr);
-      }
-      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
-      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+      const int lims[2] = {cr.len_a - tok0 - 2 * q4, cr.len_b - tok0 - 2 * q4};
       if (has_b) {
-        mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
-        mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+        mask_max_rows<2>(sr, lims, blk_ok, blocks_ok, sc, mxs);
+      } else {
+        mask_max_rows<1>(sr, lims, blk_ok, blocks_ok, sc, mxs);
+        mxs[1] = neg_inf();
       }
+      const float mxa = mxs[0], mxb = mxs[1];
       // Lazy rescale: the running max moves only when it grows by more than 8 (x256).
       float alpha_a = 1.f, alpha_b = 1.f;
       if (m_a == neg_inf()) {
@@ -958,27 +1000,11 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
         tc_fence_after();
         rescale_o(tmem, lane_addr, alpha_a, alpha_b);
       }
-      // P = 2^(s - m) as fp16 pairs (the MMA operand); rows with nothing
-      // unmasked yet (m = -inf) get zeros.  Row sums come from the tensor core.
       uint8_t* pbuf = smem + kPOff + sb * kPBuf;
-#pragma unroll 1
-      for (int x = 0; x < (has_b ? 2 : 1); ++x) {
-        const float m = x == 0 ? m_a : m_b;
-        const bool live = m != neg_inf();
-        const int mrow = x == 0 ? ma : mb;
-        uint8_t* prow = pbuf + mrow * 128 + q4 * 4;
-        const int sw = mrow & 7;
-        uint32_t pv[kStageR];
-#pragma unroll
-        for (int r = 0; r < kStageR; ++r)
-          pv[r] = pack_half2(__uint_as_float(sr[4 * r]) - m, __uint_as_float(sr[4 * r + 1]) - m);
-#pragma unroll
-        for (int r = 0; r < kStageR; ++r) pv[r] = live ? ex2_f16x2(pv[r]) : 0u;
-#pragma unroll
-        for (int r = 0; r < kStageR; ++r)
-          *reinterpret_cast<uint32_t*>(prow + (r >> 3) * kPAtom + (((r & 7) ^ sw) << 4)) = pv[r];
-        if (has_b) swap_rows_n<kStageR>(sr);
-      }
+      const float ms[2] = {m_a, m_b};
+      const int mrows[2] = {ma, mb};
+      if (has_b) store_p_rows<2>(sr, ms, mrows, pbuf, q4);
+      else store_p_rows<1>(sr, ms, mrows, pbuf, q4);
       fence_proxy_async_smem();
       tc_fence_before();
       warp_arrive(&sh->p_full[sb]);
