@@ -328,6 +328,28 @@ struct TileFeed {
     }
   }
   __device__ __forceinline__ void fetch(long long bt, int& r, int& v) const { resolve(locate(bt), r, v); }
+  // resolve() in three parts, so that several tiles' table reads are in
+  // flight together: no error is recorded (an atomic) between the loads.
+  __device__ __forceinline__ long long table_pos(const Pending& q, uint32_t& err) const {
+    if (!q.in_range || q.sid < 0 || q.sid >= p->bt_rows) return -1;
+    if (q.tile >= p->mbs) {
+      err |= kErrTooManyBlocks;
+      return -1;
+    }
+    return (long long)q.sid * p->mbs + q.tile;
+  }
+  __device__ __forceinline__ void finish(const Pending& q, long long pos, long long blk, uint32_t& err, int& r,
+                                         int& v) const {
+    r = oob_row;
+    v = 0;
+    if (pos < 0) return;  // no table entry read
+    if (blk < 0 || blk >= p->num_blocks) {
+      err |= kErrBlockIndex;
+      return;
+    }
+    v = 1;
+    r = (int)(((blk * p->num_layers + p->cur_layer) * p->num_kv_heads + q.kv_head) * kBlockTokens);
+  }
   __device__ void init(const AttnParams* pp, const PlanSmem* pps, int ngroups, int oob, long long begin,
                        long long end) {
     p = pp;
@@ -337,16 +359,23 @@ struct TileFeed {
     t_end = end;
     base = begin;
     const Pending q0 = locate(base), q1 = locate(base + 32), q2 = locate(base + 64);
-    resolve(q0, r0, v0);
-    resolve(q1, r1, v1);
-    resolve(q2, r2, v2);
+    uint32_t err = 0;
+    const long long i0 = table_pos(q0, err), i1 = table_pos(q1, err), i2 = table_pos(q2, err);
+    const long long b0 = i0 >= 0 ? (long long)__ldg(p->block_table + i0) : 0;
+    const long long b1 = i1 >= 0 ? (long long)__ldg(p->block_table + i1) : 0;
+    const long long b2 = i2 >= 0 ? (long long)__ldg(p->block_table + i2) : 0;
+    finish(q0, i0, b0, err, r0, v0);
+    finish(q1, i1, b1, err, r1, v1);
+    finish(q2, i2, b2, err, r2, v2);
+    if (err) record_error(*p, err);
   }
-  // Row and flag of tile pos + b (warp-uniform arguments, base <= pos + b < base + 64).
-  __device__ __forceinline__ void get(long long pos, int b, int& r, int& v) const {
-    const int d = (int)(pos + b - base);
-    const int rr = d < 32 ? r0 : r1, vv = d < 32 ? v0 : v1;
-    r = __shfl_sync(0xffffffffu, rr, d & 31);
-    v = __shfl_sync(0xffffffffu, vv, d & 31);
+  // Row and flag of tile pos + lane, for lanes with base <= pos + lane < base + 64.
+  __device__ __forceinline__ void get_lane(long long pos, int& r, int& v) const {
+    const int d = (int)(pos + (threadIdx.x & 31) - base);
+    const int ra = __shfl_sync(0xffffffffu, r0, d & 31), rb = __shfl_sync(0xffffffffu, r1, d & 31);
+    const int va = __shfl_sync(0xffffffffu, v0, d & 31), vb = __shfl_sync(0xffffffffu, v1, d & 31);
+    r = d < 32 ? ra : rb;
+    v = d < 32 ? va : vb;
   }
   // Drops the batches before `pos` and starts fetching the ones after.
   __device__ __forceinline__ void advance(long long pos) {
@@ -425,33 +454,36 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
     const int nst = stages_of(lo, hi);
     for (int s = 0; s < nst; ++s, ++G) {
       const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
-      int rows[kStageBlocks], valid[kStageBlocks];
-#pragma unroll
-      for (int b = 0; b < kStageBlocks; ++b) feed.get(pos, b, rows[b], valid[b]);
+      const int slot = G % kRing;
+      int row, valid;  // lane b < nblk: tile b of the stage
+      feed.get_lane(pos, row, valid);
       int waited = 1;
       if (lane == 0) {
-        const int slot = G % kRing;
         waited = wait_or_abort(sh, p, &empty[slot], (uint32_t)(((G / kRing) & 1) ^ 1));
         if (waited) {
           if (G < 100) NEB_TRACE_POINT(c, (flags ? 8 : 508) + G);
-          if (flags) {
-            const int fs = G % kFlagSlots;
-#pragma unroll
-            for (int b = 0; b < kStageBlocks; ++b) sh->blk[fs][b] = b < nblk ? valid[b] : 0;
-            mbar_arrive(&sh->flags_full[fs]);
-          }
-          uint8_t* dst = c.smem + ring_off + slot * kSlotBytes;
           mbar_arrive_expect_tx(&full[slot], (uint32_t)nblk * 2u * 2048u);
-#pragma unroll 1
-          for (int b = 0; b < nblk; ++b) {
-            tma_load_2d_hint(dst + b * 2048, tmap, &full[slot], 0, rows[b], kv_policy);
-            tma_load_2d_hint(dst + kHalf + b * 2048, tmap, &full[slot], 64, rows[b], kv_policy);
-          }
         }
       }
-      // The K warp counts the first piece in as soon as its partial is written.
-      if (lane == 0 && first && first->pending && mbar_test_wait(&sh->part_ready, 0)) first->count(c);
       waited = __shfl_sync(0xffffffffu, waited, 0);
+      if (waited) {
+        // One lane per tile issues its copies, so that a stage's loads leave together.
+        if (lane < nblk) {
+          uint8_t* dst = c.smem + ring_off + slot * kSlotBytes;
+          tma_load_2d_hint(dst + lane * 2048, tmap, &full[slot], 0, row, kv_policy);
+          tma_load_2d_hint(dst + kHalf + lane * 2048, tmap, &full[slot], 64, row, kv_policy);
+        }
+        if (flags) {
+          const int fs = G % kFlagSlots;
+          if (lane < kStageBlocks) sh->blk[fs][lane] = lane < nblk ? valid : 0;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh->flags_full[fs]);
+        }
+      }
+      // The K warp counts the first piece in as soon as its partial is written
+      // (which piece that is, it works out once the first loads are on their way).
+      if (first && G == 0) first->init(c);
+      if (lane == 0 && first && first->pending && mbar_test_wait(&sh->part_ready, 0)) first->count(c);
       if (!waited) {
         ok = false;
         break;
@@ -1102,7 +1134,7 @@ __global__ void __launch_bounds__(kVThreads, 1)
 
   if (warp == kKWarp) {
     FirstSplit first;
-    first.init(c);
+    first.pending = false;
     producer(c, &tmap_k, sh->k_full, sh->k_empty, kKOff, 1, &first);
   } else if (warp == kVWarp) {
     producer(c, &tmap_v, sh->v_full, sh->v_empty, kVOff, 0, nullptr);

@@ -71,6 +71,10 @@ SHAPES = {
     # group longer than one MMA tile can hold (depth 40 -> 41 rows x GQA 4 > 128)
     "verify_deep": dict(num_requests=2, depth=40, ctx_lo=50, ctx_hi=300, num_q_heads=32, num_kv_heads=8,
                         pool_blocks=64),
+    # one unit cut into a piece per CTA: every piece claims at its end and one
+    # merger waits for all the others' partials
+    "one_unit_all_ctas": dict(num_requests=1, depth=4, ctx_lo=3000, ctx_hi=3000, num_q_heads=4, num_kv_heads=1,
+                              pool_blocks=200),
     # GQA 1 and GQA 8
     "mha": dict(num_requests=5, depth=2, ctx_lo=10, ctx_hi=400, num_q_heads=4, num_kv_heads=4, pool_blocks=200),
     "gqa8": dict(num_requests=5, depth=3, ctx_lo=10, ctx_hi=400, num_q_heads=16, num_kv_heads=2,
