@@ -70,9 +70,10 @@ constexpr int kPVWarp = 7;
 constexpr int kStageBlocks = 4;                           // 16-token KV blocks per stage
 constexpr int kStageCols = kStageBlocks * kBlockTokens;   // tokens per stage: the S tile's N
 constexpr int kStageR = kStageCols / 8;                   // 8-column groups of an S tile
-constexpr int kRing = 4;                                  // depth of the K ring and of the V ring
+constexpr int kKRing = 4;                                 // depth of the K ring
+constexpr int kVRing = 4;                                 // depth of the V ring
 constexpr int kSBufs = 4;                                 // S tiles in TMEM (the S issuer runs ahead)
-constexpr int kFlagSlots = kRing + kSBufs;                // block-flag ring (see the K producer)
+constexpr int kFlagSlots = kKRing + kSBufs;                // block-flag ring (see the K producer)
 constexpr int kMaxQRows = 64;                             // query rows per unit: the MMA's M
 constexpr int kMaxGqa = 16;                               // a row's heads fit one 16-row chunk
 constexpr uint32_t kTmemCols = 512;
@@ -91,10 +92,10 @@ constexpr uint32_t kQOff = 0;                      // two Q buffers
 constexpr uint32_t kHalf = kStageBlocks * 2048;    // one 64-column half of K or V of a stage
 constexpr uint32_t kSlotBytes = 2 * kHalf;         // a ring slot: both halves of K (or V)
 constexpr uint32_t kKOff = kQOff + 2 * kQBuf;
-constexpr uint32_t kVOff = kKOff + kRing * kSlotBytes;
+constexpr uint32_t kVOff = kKOff + kKRing * kSlotBytes;
 constexpr uint32_t kPAtom = kMaxQRows * 128;       // 64 rows x 64 fp16 of P (one swizzle column)
 constexpr uint32_t kPBuf = ((kStageCols + 63) / 64) * kPAtom;
-constexpr uint32_t kPOff = kVOff + kRing * kSlotBytes;
+constexpr uint32_t kPOff = kVOff + kVRing * kSlotBytes;
 constexpr uint32_t kOnesOff = kPOff + 2 * kPBuf;   // 16 rows x 128 B of fp16 ones
 constexpr uint32_t kBarOff = kOnesOff + 2048;
 constexpr uint32_t kPlanOff = kBarOff + 1024;
@@ -105,11 +106,27 @@ static_assert(kHalf % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 constexpr int kVerifyMaxRows = ((232448 - 1024 - 256 - (int)kPlanOff) / 4 - 8) / 3 - 1;
 static_assert(kVerifyMaxRows >= 1024, "room for the plan of a large verify batch");
 
+struct VerifyShared;
+
+// What every role needs to know about the launch and its own CTA.
+struct Ctx {
+  const AttnParams* p;
+  VerifyShared* sh;
+  uint8_t* smem;
+  PlanSmem ps;
+  int ng, hk, gqa, oob_row;
+  long long total, workers, w, t_begin, t_end;
+  CostSplit split;  // which worker owns which tiles
+  uint32_t tmem;
+  unsigned long long* trace;  // timeline buffer row of this CTA (builds with NEB_TRACE only)
+};
+
 struct VerifyShared {
-  uint64_t k_full[kRing];        // K landed
-  uint64_t k_empty[kRing];       // S of the slot's stage completed
-  uint64_t v_full[kRing];        // V landed
-  uint64_t v_empty[kRing];       // P V of the slot's stage completed
+  Ctx ctx;                       // the launch context, written once by thread 0
+  uint64_t k_full[kKRing];       // K landed
+  uint64_t k_empty[kKRing];      // S of the slot's stage completed
+  uint64_t v_full[kVRing];       // V landed
+  uint64_t v_empty[kVRing];      // P V of the slot's stage completed
   uint64_t flags_full[kFlagSlots];
   uint64_t s_full[kSBufs];
   uint64_t s_empty[kSBufs];
@@ -136,19 +153,6 @@ __host__ __device__ inline size_t verify_smem_bytes(int num_rows) {
 struct VerifyArgs {
   AttnParams p;
   int oob_row;  // first row past the end of the K/V tensor maps (loads there return zeros)
-};
-
-// What every role needs to know about the launch and its own CTA.
-struct Ctx {
-  const AttnParams* p;
-  VerifyShared* sh;
-  uint8_t* smem;
-  PlanSmem ps;
-  int ng, hk, gqa, oob_row;
-  long long total, workers, w, t_begin, t_end;
-  CostSplit split;  // which worker owns which tiles
-  uint32_t tmem;
-  unsigned long long* trace;  // timeline buffer row of this CTA (builds with NEB_TRACE only)
 };
 
 // Timeline hooks: empty unless the library is built with -DNEB_TRACE, in which
@@ -426,14 +430,15 @@ struct FirstSplit {
 
 // ------------------------------------------------------------------ producers
 // One function serves the K warp (flags != 0: it also publishes the block
-// flags) and the V warp.  Slot G % kRing frees when the MMA that read it (S for
-// K, P V for V) of stage G - kRing is done.  The block flags of stage G go to
+// flags) and the V warp, over a ring of `ring` slots (kKRing, kVRing).  Slot
+// G % ring frees when the MMA that read it (S for K, P V for V) of stage
+// G - ring is done.  The block flags of stage G go to
 // flag slot G % kFlagSlots: its previous reader, the softmax of stage
 // G - kFlagSlots, reads the flags before it releases S of that stage, which
-// S(G - kRing) (issued only once S buffer (G - kRing) % kSBufs was released by
-// the softmax of stage G - kRing - kSBufs), and so this load, had to wait for.
+// S(G - kKRing) (issued only once S buffer (G - kKRing) % kSBufs was released
+// by the softmax of stage G - kKRing - kSBufs), and so this load, had to wait for.
 __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uint64_t* full, uint64_t* empty,
-                                      uint32_t ring_off, int flags, FirstSplit* first) {
+                                      uint32_t ring_off, int ring, int flags, FirstSplit* first) {
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
   const int lane = threadIdx.x & 31;
@@ -447,19 +452,19 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
   cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
   int g, h, lo, hi, nb;
   long long ustart;
-  int G = 0;
+  int G = 0, slot = 0;  // stage, its ring slot and the parity of the slot's current use
+  uint32_t phase = 0;
   long long pos = c.t_begin;
   bool ok = true;
   while (ok && cur.next(g, h, lo, hi, nb, ustart)) {
     const int nst = stages_of(lo, hi);
     for (int s = 0; s < nst; ++s, ++G) {
       const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
-      const int slot = G % kRing;
       int row, valid;  // lane b < nblk: tile b of the stage
       feed.get_lane(pos, row, valid);
       int waited = 1;
       if (lane == 0) {
-        waited = wait_or_abort(sh, p, &empty[slot], (uint32_t)(((G / kRing) & 1) ^ 1));
+        waited = wait_or_abort(sh, p, &empty[slot], phase ^ 1u);
         if (waited) {
           if (G < 100) NEB_TRACE_POINT(c, (flags ? 8 : 508) + G);
           mbar_arrive_expect_tx(&full[slot], (uint32_t)nblk * 2u * 2048u);
@@ -490,14 +495,18 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
       }
       pos += nblk;
       feed.advance(pos);
+      if (++slot == ring) {
+        slot = 0;
+        phase ^= 1u;
+      }
     }
   }
   if (lane == 0 && first && first->pending && wait_or_abort(sh, p, &sh->part_ready, 0)) first->count(c);
   // Wait (bounded) for every copy this warp issued before the CTA can exit.
   if (lane == 0)
 #pragma unroll 1
-    for (int Gi = (G > kRing ? G - kRing : 0); Gi < G; ++Gi)
-      mbar_wait(&full[Gi % kRing], (uint32_t)((Gi / kRing) & 1), kWaitLimit);
+    for (int Gi = (G > ring ? G - ring : 0); Gi < G; ++Gi)
+      mbar_wait(&full[Gi % ring], (uint32_t)((Gi / ring) & 1), kWaitLimit);
 }
 
 
@@ -574,8 +583,8 @@ __device__ __noinline__ void s_issuer(const Ctx& c, const CUtensorMap* tmap_q) {
       break;
     const uint32_t qb = q_base + b * kQBuf;
     for (int s = 0; s < nst; ++s, ++G) {
-      const int slot = G % kRing, sb = G % kSBufs;
-      if (!wait_or_abort(sh, p, &sh->k_full[slot], (uint32_t)((G / kRing) & 1)) ||
+      const int slot = G % kKRing, sb = G % kSBufs;
+      if (!wait_or_abort(sh, p, &sh->k_full[slot], (uint32_t)((G / kKRing) & 1)) ||
           !wait_or_abort(sh, p, &sh->s_empty[sb], (uint32_t)(((G / kSBufs) & 1) ^ 1))) {
         ok = false;
         break;
@@ -627,9 +636,9 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
   for (int piece = 0; ok && cur.next(g, h, lo, hi, nb, ustart); ++piece) {
     const int nst = stages_of(lo, hi);
     for (int s = 0; s < nst; ++s, ++G) {
-      const int slot = G % kRing, sb = G & 1;
+      const int slot = G % kVRing, sb = G & 1;
       if (!wait_or_abort(sh, p, &sh->p_full[sb], (uint32_t)((G >> 1) & 1)) ||
-          !wait_or_abort(sh, p, &sh->v_full[slot], (uint32_t)((G / kRing) & 1)) ||
+          !wait_or_abort(sh, p, &sh->v_full[slot], (uint32_t)((G / kVRing) & 1)) ||
           (s == 0 && piece > 0 && !wait_or_abort(sh, p, &sh->o_empty, (uint32_t)((piece - 1) & 1)))) {
         ok = false;
         break;
@@ -1097,9 +1106,11 @@ __global__ void __launch_bounds__(kVThreads, 1)
   c.t_end = c.split.begin(c.w + 1);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kRing; ++i) {
+    for (int i = 0; i < kKRing; ++i) {
       mbar_init(&sh->k_full[i], 1);
       mbar_init(&sh->k_empty[i], 1);
+    }
+    for (int i = 0; i < kVRing; ++i) {
       mbar_init(&sh->v_full[i], 1);
       mbar_init(&sh->v_empty[i], 1);
     }
@@ -1126,32 +1137,37 @@ __global__ void __launch_bounds__(kVThreads, 1)
     tmem_alloc(&sh->tmem_base, kTmemCols);
     tmem_relinquish();
   }
+  // The roles read the context from shared memory (one copy per CTA) rather
+  // than from a stack copy per thread, which would live in local memory.
+  if (threadIdx.x == 0) sh->ctx = c;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  c.tmem = sh->tmem_base;
-  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 2);
+  if (threadIdx.x == 0) sh->ctx.tmem = sh->tmem_base;
+  __syncthreads();
+  const Ctx& cs = sh->ctx;
+  if (threadIdx.x == 0) NEB_TRACE_POINT(cs, 2);
 
   if (warp == kKWarp) {
     FirstSplit first;
     first.pending = false;
-    producer(c, &tmap_k, sh->k_full, sh->k_empty, kKOff, 1, &first);
+    producer(cs, &tmap_k, sh->k_full, sh->k_empty, kKOff, kKRing, 1, &first);
   } else if (warp == kVWarp) {
-    producer(c, &tmap_v, sh->v_full, sh->v_empty, kVOff, 0, nullptr);
+    producer(cs, &tmap_v, sh->v_full, sh->v_empty, kVOff, kVRing, 0, nullptr);
   } else if (warp == kSWarp) {
-    if (lane == 0) s_issuer(c, &tmap_q);
+    if (lane == 0) s_issuer(cs, &tmap_q);
   } else if (warp == kPVWarp) {
-    if (lane == 0) pv_issuer(c);
+    if (lane == 0) pv_issuer(cs);
   } else {
-    softmax_role(c);
-    if (warp == kSoftmaxWarp0 && lane == 0) NEB_TRACE_POINT(c, 3);
+    softmax_role(cs);
+    if (warp == kSoftmaxWarp0 && lane == 0) NEB_TRACE_POINT(cs, 3);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == kSWarp) tmem_dealloc(c.tmem, kTmemCols);
-  if (!aborted(sh) && sh->first_last) finish_first_unit(c);
-  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 4);
+  if (warp == kSWarp) tmem_dealloc(cs.tmem, kTmemCols);
+  if (!aborted(sh) && sh->first_last) finish_first_unit(cs);
+  if (threadIdx.x == 0) NEB_TRACE_POINT(cs, 4);
 }
 
 // ------------------------------------------------------------------ host side
