@@ -70,10 +70,11 @@ constexpr int kPVWarp = 7;
 constexpr int kStageBlocks = 4;                           // 16-token KV blocks per stage
 constexpr int kStageCols = kStageBlocks * kBlockTokens;   // tokens per stage: the S tile's N
 constexpr int kStageR = kStageCols / 8;                   // 8-column groups of an S tile
-constexpr int kKRing = 4;                                 // depth of the K ring
-constexpr int kVRing = 4;                                 // depth of the V ring
+constexpr int kSlotStages = 2;                            // stages per K (V) ring slot: one TMA phase
+constexpr int kKRing = 2;                                 // slots of the K ring
+constexpr int kVRing = 2;                                 // slots of the V ring
 constexpr int kSBufs = 4;                                 // S tiles in TMEM (the S issuer runs ahead)
-constexpr int kFlagSlots = kKRing + kSBufs;                // block-flag ring (see the K producer)
+constexpr int kFlagSlots = kSlotStages * kKRing + kSBufs;  // block-flag ring (see the K producer)
 constexpr int kMaxQRows = 64;                             // query rows per unit: the MMA's M
 constexpr int kMaxGqa = 16;                               // a row's heads fit one 16-row chunk
 constexpr uint32_t kTmemCols = 512;
@@ -90,7 +91,8 @@ constexpr uint32_t kQHalf = kMaxQRows * 128;       // one 64-column half of Q
 constexpr uint32_t kQBuf = 2 * kQHalf;             // Q of one piece
 constexpr uint32_t kQOff = 0;                      // two Q buffers
 constexpr uint32_t kHalf = kStageBlocks * 2048;    // one 64-column half of K or V of a stage
-constexpr uint32_t kSlotBytes = 2 * kHalf;         // a ring slot: both halves of K (or V)
+constexpr uint32_t kStageBytes = 2 * kHalf;        // one stage of K (or V): both halves
+constexpr uint32_t kSlotBytes = kSlotStages * kStageBytes;  // a ring slot
 constexpr uint32_t kKOff = kQOff + 2 * kQBuf;
 constexpr uint32_t kVOff = kKOff + kKRing * kSlotBytes;
 constexpr uint32_t kPAtom = kMaxQRows * 128;       // 64 rows x 64 fp16 of P (one swizzle column)
@@ -123,10 +125,10 @@ struct Ctx {
 
 struct VerifyShared {
   Ctx ctx;                       // the launch context, written once by thread 0
-  uint64_t k_full[kKRing];       // K landed
-  uint64_t k_empty[kKRing];      // S of the slot's stage completed
-  uint64_t v_full[kVRing];       // V landed
-  uint64_t v_empty[kVRing];      // P V of the slot's stage completed
+  uint64_t k_full[kKRing];       // K of the slot's stages landed
+  uint64_t k_empty[kKRing];      // S of the slot's stages completed (one arrival per stage)
+  uint64_t v_full[kVRing];       // V of the slot's stages landed
+  uint64_t v_empty[kVRing];      // P V of the slot's stages completed (one arrival per stage)
   uint64_t flags_full[kFlagSlots];
   uint64_t s_full[kSBufs];
   uint64_t s_empty[kSBufs];
@@ -373,9 +375,9 @@ struct TileFeed {
     finish(q2, i2, b2, err, r2, v2);
     if (err) record_error(*p, err);
   }
-  // Row and flag of tile pos + lane, for lanes with base <= pos + lane < base + 64.
-  __device__ __forceinline__ void get_lane(long long pos, int& r, int& v) const {
-    const int d = (int)(pos + (threadIdx.x & 31) - base);
+  // Row and flag of tile pos + b (b per lane), for base <= pos + b < base + 64.
+  __device__ __forceinline__ void get_lane(long long pos, int b, int& r, int& v) const {
+    const int d = (int)(pos + b - base);
     const int ra = __shfl_sync(0xffffffffu, r0, d & 31), rb = __shfl_sync(0xffffffffu, r1, d & 31);
     const int va = __shfl_sync(0xffffffffu, v0, d & 31), vb = __shfl_sync(0xffffffffu, v1, d & 31);
     r = d < 32 ? ra : rb;
@@ -430,13 +432,16 @@ struct FirstSplit {
 
 // ------------------------------------------------------------------ producers
 // One function serves the K warp (flags != 0: it also publishes the block
-// flags) and the V warp, over a ring of `ring` slots (kKRing, kVRing).  Slot
-// G % ring frees when the MMA that read it (S for K, P V for V) of stage
-// G - ring is done.  The block flags of stage G go to
-// flag slot G % kFlagSlots: its previous reader, the softmax of stage
-// G - kFlagSlots, reads the flags before it releases S of that stage, which
-// S(G - kKRing) (issued only once S buffer (G - kKRing) % kSBufs was released
-// by the softmax of stage G - kKRing - kSBufs), and so this load, had to wait for.
+// flags) and the V warp, over a ring of `ring` slots (kKRing, kVRing) of
+// kSlotStages stages each: one TMA phase per slot, so that each wait and
+// transaction count covers 32 KB.  Stage G sits in slot (G / 2) % ring; the
+// slot frees when the MMAs that read its stages (S for K, P V for V) are done.
+// The block flags of stage G go to flag slot G % kFlagSlots.  Before the flags
+// of stages G and G + 1 are written, the slot that held stages G - 2*kKRing and
+// G - 2*kKRing + 1 has been freed, so S of those stages was issued, which
+// needed S buffer (G - 2*kKRing + 1) % kSBufs released by the softmax of stage
+// G - 2*kKRing + 1 - kSBufs, and the softmax reads a stage's flags before it
+// releases its S: flag slots with kFlagSlots >= 2*kKRing + kSBufs are free.
 __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uint64_t* full, uint64_t* empty,
                                       uint32_t ring_off, int ring, int flags, FirstSplit* first) {
   const AttnParams& p = *c.p;
@@ -448,65 +453,84 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
   const uint64_t kv_policy = l2_evict_first_policy();
   TileFeed feed;
   feed.init(&p, &c.ps, c.ng, c.oob_row, c.t_begin, c.t_end);
+  // The worker's stages in order, as block counts: each piece cut into
+  // kStageBlocks-block stages (the last one of a piece may be shorter).
   PieceCursor cur;
   cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
-  int g, h, lo, hi, nb;
-  long long ustart;
-  int G = 0, slot = 0;  // stage, its ring slot and the parity of the slot's current use
-  uint32_t phase = 0;
+  int s_lo = 0, s_hi = 0;
+  auto next_stage = [&](int& nblk) -> bool {
+    if (s_lo >= s_hi) {
+      int g, h, nb;
+      long long ustart;
+      if (!cur.next(g, h, s_lo, s_hi, nb, ustart)) return false;
+    }
+    nblk = min(kStageBlocks, s_hi - s_lo);
+    s_lo += nblk;
+    return true;
+  };
+  // Lane l < 16 carries box (l & 7) of the slot's stage l >> 3: tile l & 3,
+  // half (l >> 2) & 1.
+  const int st = lane >> 3, b = lane & (kStageBlocks - 1), hf = (lane >> 2) & 1;
+  int G = 0, slot = 0, used = 0;  // first stage of the slot, the slot, slots filled so far
+  uint32_t phase = 0;             // parity of the slot's current use
   long long pos = c.t_begin;
-  bool ok = true;
-  while (ok && cur.next(g, h, lo, hi, nb, ustart)) {
-    const int nst = stages_of(lo, hi);
-    for (int s = 0; s < nst; ++s, ++G) {
-      const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
-      int row, valid;  // lane b < nblk: tile b of the stage
-      feed.get_lane(pos, row, valid);
-      int waited = 1;
-      if (lane == 0) {
-        waited = wait_or_abort(sh, p, &empty[slot], phase ^ 1u);
-        if (waited) {
-          if (G < 100) NEB_TRACE_POINT(c, (flags ? 8 : 508) + G);
-          mbar_arrive_expect_tx(&full[slot], (uint32_t)nblk * 2u * 2048u);
-        }
-      }
-      waited = __shfl_sync(0xffffffffu, waited, 0);
+  int n0 = 0;
+  bool more = next_stage(n0);
+  while (more) {
+    int n1 = 0;
+    const bool two = next_stage(n1);
+    const int nst = two ? 2 : 1;
+    const int nb_st = st ? n1 : n0;
+    int row, valid;
+    feed.get_lane(pos, (st ? n0 : 0) + b, row, valid);
+    int waited = 1;
+    if (lane == 0) {
+      if (G < 90) NEB_TRACE_POINT(c, (flags ? 1010 : 1110) + G);
+      waited = wait_or_abort(sh, p, &empty[slot], phase ^ 1u);
       if (waited) {
-        // One lane per tile issues its copies, so that a stage's loads leave together.
-        if (lane < nblk) {
-          uint8_t* dst = c.smem + ring_off + slot * kSlotBytes;
-          tma_load_2d_hint(dst + lane * 2048, tmap, &full[slot], 0, row, kv_policy);
-          tma_load_2d_hint(dst + kHalf + lane * 2048, tmap, &full[slot], 64, row, kv_policy);
+        if (G < 99) {
+          NEB_TRACE_POINT(c, (flags ? 8 : 508) + G);
+          NEB_TRACE_POINT(c, (flags ? 8 : 508) + G + 1);
         }
-        if (flags) {
-          const int fs = G % kFlagSlots;
-          if (lane < kStageBlocks) sh->blk[fs][lane] = lane < nblk ? valid : 0;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sh->flags_full[fs]);
-        }
-      }
-      // The K warp counts the first piece in as soon as its partial is written
-      // (which piece that is, it works out once the first loads are on their way).
-      if (first && G == 0) first->init(c);
-      if (lane == 0 && first && first->pending && mbar_test_wait(&sh->part_ready, 0)) first->count(c);
-      if (!waited) {
-        ok = false;
-        break;
-      }
-      pos += nblk;
-      feed.advance(pos);
-      if (++slot == ring) {
-        slot = 0;
-        phase ^= 1u;
+        mbar_arrive_expect_tx(&full[slot], (uint32_t)(n0 + n1) * 2u * 2048u);
       }
     }
+    waited = __shfl_sync(0xffffffffu, waited, 0);
+    if (waited) {
+      // One lane per 64-column box, so that the slot's loads leave together.
+      if (st < nst && b < nb_st)
+        tma_load_2d_hint(c.smem + ring_off + slot * kSlotBytes + st * kStageBytes + hf * kHalf + b * 2048, tmap,
+                         &full[slot], 64 * hf, row, kv_policy);
+      if (flags) {
+        if (st < nst && hf == 0) sh->blk[(G + st) % kFlagSlots][b] = b < nb_st ? valid : 0;
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sh->flags_full[G % kFlagSlots]);
+          if (two) mbar_arrive(&sh->flags_full[(G + 1) % kFlagSlots]);
+        }
+      }
+    }
+    // The K warp counts the first piece in as soon as its partial is written
+    // (which piece that is, it works out once the first loads are on their way).
+    if (first && G == 0) first->init(c);
+    if (lane == 0 && first && first->pending && mbar_test_wait(&sh->part_ready, 0)) first->count(c);
+    if (!waited) break;
+    ++used;
+    pos += n0 + n1;
+    feed.advance(pos);
+    G += nst;
+    if (++slot == ring) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    more = two && next_stage(n0);
   }
   if (lane == 0 && first && first->pending && wait_or_abort(sh, p, &sh->part_ready, 0)) first->count(c);
   // Wait (bounded) for every copy this warp issued before the CTA can exit.
   if (lane == 0)
 #pragma unroll 1
-    for (int Gi = (G > ring ? G - ring : 0); Gi < G; ++Gi)
-      mbar_wait(&full[Gi % ring], (uint32_t)((Gi / ring) & 1), kWaitLimit);
+    for (int u = (used > ring ? used - ring : 0); u < used; ++u)
+      mbar_wait(&full[u % ring], (uint32_t)((u / ring) & 1), kWaitLimit);
 }
 
 
@@ -583,8 +607,9 @@ __device__ __noinline__ void s_issuer(const Ctx& c, const CUtensorMap* tmap_q) {
       break;
     const uint32_t qb = q_base + b * kQBuf;
     for (int s = 0; s < nst; ++s, ++G) {
-      const int slot = G % kKRing, sb = G % kSBufs;
-      if (!wait_or_abort(sh, p, &sh->k_full[slot], (uint32_t)((G / kKRing) & 1)) ||
+      const int slot = (G / kSlotStages) % kKRing, sb = G % kSBufs;
+      if (G < 90) NEB_TRACE_POINT(c, 1210 + G);
+      if (!wait_or_abort(sh, p, &sh->k_full[slot], (uint32_t)((G / kSlotStages / kKRing) & 1)) ||
           !wait_or_abort(sh, p, &sh->s_empty[sb], (uint32_t)(((G / kSBufs) & 1) ^ 1))) {
         ok = false;
         break;
@@ -593,13 +618,14 @@ __device__ __noinline__ void s_issuer(const Ctx& c, const CUtensorMap* tmap_q) {
       tc_fence_after();
       const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
       const uint32_t idesc_s = idesc_f16_f32(kMaxQRows, 16 * nblk, false, false);
-      const uint32_t kst = k_base + slot * kSlotBytes;
-#pragma unroll 1
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t a = smem_desc_sw128(qb + (kk >> 2) * kQHalf + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = smem_desc_sw128(kst + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-        mma_f16(tmem + sb * kSBuf, a, bd, idesc_s, kk > 0 ? 1u : 0u);
-      }
+      const uint32_t kst = k_base + slot * kSlotBytes + (G % kSlotStages) * kStageBytes;
+      // Descriptors of the eight K=16 steps: the base's address field plus
+      // a constant (shared-memory addresses / 16 stay below 2^14).
+      const uint64_t a0 = smem_desc_sw128(qb, 16, 1024), b0 = smem_desc_sw128(kst, 16, 1024);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16(tmem + sb * kSBuf, a0 + (((kk >> 2) * kQHalf + (kk & 3) * 32) >> 4),
+                b0 + (((kk >> 2) * kHalf + (kk & 3) * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
       mma_commit(&sh->s_full[sb]);
       mma_commit(&sh->k_empty[slot]);
       if (s == nst - 1) mma_commit(&sh->q_empty[b]);
@@ -636,9 +662,10 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
   for (int piece = 0; ok && cur.next(g, h, lo, hi, nb, ustart); ++piece) {
     const int nst = stages_of(lo, hi);
     for (int s = 0; s < nst; ++s, ++G) {
-      const int slot = G % kVRing, sb = G & 1;
+      const int slot = (G / kSlotStages) % kVRing, sb = G & 1;
+      if (G < 90) NEB_TRACE_POINT(c, 1310 + G);
       if (!wait_or_abort(sh, p, &sh->p_full[sb], (uint32_t)((G >> 1) & 1)) ||
-          !wait_or_abort(sh, p, &sh->v_full[slot], (uint32_t)((G / kVRing) & 1)) ||
+          !wait_or_abort(sh, p, &sh->v_full[slot], (uint32_t)((G / kSlotStages / kVRing) & 1)) ||
           (s == 0 && piece > 0 && !wait_or_abort(sh, p, &sh->o_empty, (uint32_t)((piece - 1) & 1)))) {
         ok = false;
         break;
@@ -646,14 +673,17 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
       if (G < 100) NEB_TRACE_POINT(c, 208 + G);
       tc_fence_after();
       const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
-      const uint32_t vst = v_base + slot * kSlotBytes;
-#pragma unroll 1
-      for (int kb = 0; kb < nblk; ++kb) {
-        const uint64_t a = smem_desc_sw128(p_base + sb * kPBuf + (kb >> 2) * kPAtom + (kb & 3) * 32, 16, 1024);
-        const uint64_t b = smem_desc_sw128(vst + kb * 2048, kHalf, 1024);
-        const uint32_t acc = (s == 0 && kb == 0) ? 0u : 1u;
-        mma_f16(tmem + kOCol, a, b, idesc_pv, acc);
-        mma_f16(tmem + kSumCol, a, smem_desc_sw128(ones_base + (kb & 3) * 32, 16, 1024), idesc_sum, acc);
+      const uint32_t vst = v_base + slot * kSlotBytes + (G % kSlotStages) * kStageBytes;
+      const uint64_t pa0 = smem_desc_sw128(p_base + sb * kPBuf, 16, 1024);
+      const uint64_t vb0 = smem_desc_sw128(vst, kHalf, 1024), ob0 = smem_desc_sw128(ones_base, 16, 1024);
+#pragma unroll
+      for (int kb = 0; kb < kStageBlocks; ++kb) {
+        if (kb < nblk) {
+          const uint64_t a = pa0 + (((kb >> 2) * kPAtom + (kb & 3) * 32) >> 4);
+          const uint32_t acc = (s == 0 && kb == 0) ? 0u : 1u;
+          mma_f16(tmem + kOCol, a, vb0 + ((kb * 2048) >> 4), idesc_pv, acc);
+          mma_f16(tmem + kSumCol, a, ob0 + (((kb & 3) * 32) >> 4), idesc_sum, acc);
+        }
       }
       mma_commit(&sh->v_empty[slot]);
       mma_commit(&sh->pv_done[sb]);
@@ -1108,11 +1138,11 @@ __global__ void __launch_bounds__(kVThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kKRing; ++i) {
       mbar_init(&sh->k_full[i], 1);
-      mbar_init(&sh->k_empty[i], 1);
+      mbar_init(&sh->k_empty[i], kSlotStages);
     }
     for (int i = 0; i < kVRing; ++i) {
       mbar_init(&sh->v_full[i], 1);
-      mbar_init(&sh->v_empty[i], 1);
+      mbar_init(&sh->v_empty[i], kSlotStages);
     }
     for (int i = 0; i < kFlagSlots; ++i) mbar_init(&sh->flags_full[i], 1);
     for (int i = 0; i < kSBufs; ++i) {
