@@ -80,7 +80,6 @@ constexpr int kMaxGqa = 16;                               // a row's heads fit o
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSBuf = 64;                            // S tile b at columns 64*b
 constexpr uint32_t kOCol = 256;                           // O: 128 columns
-constexpr uint32_t kSumCol = 384;                         // P x ones: every column holds the row sum
 constexpr long long kWaitLimit = 4000000000LL;
 constexpr int kMaxDirectOthers = 3;                      // direct merge: at most 3 other pieces
 constexpr int kPieceCost = 8;                             // a piece's fixed cost, in tiles (plan.cuh CostSplit)
@@ -98,8 +97,7 @@ constexpr uint32_t kVOff = kKOff + kKRing * kSlotBytes;
 constexpr uint32_t kPAtom = kMaxQRows * 128;       // 64 rows x 64 fp16 of P (one swizzle column)
 constexpr uint32_t kPBuf = ((kStageCols + 63) / 64) * kPAtom;
 constexpr uint32_t kPOff = kVOff + kVRing * kSlotBytes;
-constexpr uint32_t kOnesOff = kPOff + 2 * kPBuf;   // 16 rows x 128 B of fp16 ones
-constexpr uint32_t kBarOff = kOnesOff + 2048;
+constexpr uint32_t kBarOff = kPOff + 2 * kPBuf;
 constexpr uint32_t kPlanOff = kBarOff + 1024;
 static_assert(kHalf % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 
@@ -649,9 +647,7 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
   VerifyShared* sh = c.sh;
   const uint32_t v_base = smem_u32(c.smem + kVOff);
   const uint32_t p_base = smem_u32(c.smem + kPOff);
-  const uint32_t ones_base = smem_u32(c.smem + kOnesOff);
   const uint32_t idesc_pv = idesc_f16_f32(kMaxQRows, 128, false, true);
-  const uint32_t idesc_sum = idesc_f16_f32(kMaxQRows, 16, false, false);
   const uint32_t tmem = c.tmem;
   PieceCursor cur;
   cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
@@ -675,14 +671,13 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
       const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
       const uint32_t vst = v_base + slot * kSlotBytes + (G % kSlotStages) * kStageBytes;
       const uint64_t pa0 = smem_desc_sw128(p_base + sb * kPBuf, 16, 1024);
-      const uint64_t vb0 = smem_desc_sw128(vst, kHalf, 1024), ob0 = smem_desc_sw128(ones_base, 16, 1024);
+      const uint64_t vb0 = smem_desc_sw128(vst, kHalf, 1024);
 #pragma unroll
       for (int kb = 0; kb < kStageBlocks; ++kb) {
         if (kb < nblk) {
           const uint64_t a = pa0 + (((kb >> 2) * kPAtom + (kb & 3) * 32) >> 4);
           const uint32_t acc = (s == 0 && kb == 0) ? 0u : 1u;
           mma_f16(tmem + kOCol, a, vb0 + ((kb * 2048) >> 4), idesc_pv, acc);
-          mma_f16(tmem + kSumCol, a, ob0 + (((kb & 3) * 32) >> 4), idesc_sum, acc);
         }
       }
       mma_commit(&sh->v_empty[slot]);
@@ -694,8 +689,7 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
 }
 
 // -------------------------------------------------------------------- softmax
-// O and the row sums times (alpha_a, alpha_b), in TMEM (rare: a row's max grew
-// by more than 2^8).
+// O times (alpha_a, alpha_b), in TMEM (rare: a row's max grew by more than 2^8).
 __device__ __noinline__ void rescale_o(uint32_t tmem, uint32_t lane_addr, float alpha_a, float alpha_b) {
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
@@ -706,11 +700,6 @@ __device__ __noinline__ void rescale_o(uint32_t tmem, uint32_t lane_addr, float 
     scale_rows(orr, 8, alpha_a, alpha_b);
     tmem_st_16x256b_x8(oaddr, orr);
   }
-  uint32_t srr[8];
-  tmem_ld_16x256b_x2(tmem + kSumCol + lane_addr, srr);
-  tmem_wait_ld();
-  scale_rows(srr, 2, alpha_a, alpha_b);
-  tmem_st_16x256b_x2(tmem + kSumCol + lane_addr, srr);
   tmem_wait_st();
 }
 
@@ -729,7 +718,7 @@ struct SoftmaxRows {
 // softmax warps merge the partials.  The first piece's partial is counted in
 // by the K warp.  The PV issuer may reuse O once it has been read.
 __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, int G_last, float m_a, float m_b,
-                                            bool last_piece) {
+                                            float l_a, float l_b, bool last_piece) {
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -758,10 +747,11 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
   if (!wait_or_abort(sh, p, &sh->pv_done[G_last & 1], (uint32_t)((G_last >> 1) & 1))) return false;
   if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1508 + G_last);
   tc_fence_after();
-  uint32_t sums[8];
-  tmem_ld_16x256b_x2(c.tmem + kSumCol + lane_addr, sums);
-  tmem_wait_ld();
-  const float l_a = __uint_as_float(sums[0]), l_b = __uint_as_float(sums[2]);
+  // Row sums: each of a row's four threads holds the sum of its columns.
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
   if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1900 + G_last);
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
@@ -921,10 +911,11 @@ __device__ __forceinline__ void mask_max_rows(uint32_t* sr, const int* lim, int 
 
 // P = 2^(s - m) as fp16 pairs (the MMA operand) into the swizzled P tile for
 // the kRows rows of this thread (MMA rows mrow[x]); rows with nothing
-// unmasked yet (m = -inf) get zeros.
+// unmasked yet (m = -inf) get zeros.  lsum[x] += the fp32 sum of the fp16
+// values stored (the row sum is the sum of exactly the P the MMA reads).
 template <int kRows>
 __device__ __forceinline__ void store_p_rows(const uint32_t* sr, const float* m, const int* mrow, uint8_t* pbuf,
-                                             int q4) {
+                                             int q4, float* lsum) {
   uint32_t pv[kRows][kStageR];
 #pragma unroll
   for (int x = 0; x < kRows; ++x)
@@ -935,6 +926,16 @@ __device__ __forceinline__ void store_p_rows(const uint32_t* sr, const float* m,
   for (int x = 0; x < kRows; ++x)
 #pragma unroll
     for (int r = 0; r < kStageR; ++r) pv[x][r] = m[x] != neg_inf() ? ex2_f16x2(pv[x][r]) : 0u;
+#pragma unroll
+  for (int x = 0; x < kRows; ++x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < kStageR; ++r) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pv[x][r]));
+      acc += f.x + f.y;
+    }
+    lsum[x] += acc;
+  }
 #pragma unroll
   for (int x = 0; x < kRows; ++x) {
     uint8_t* prow = pbuf + mrow[x] * 128 + q4 * 4;
@@ -959,15 +960,11 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
   const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
   const float sc = p.scale_log2;
   const int gqa = c.gqa;
-  // Clear P once (rows no unit writes must hold finite values) and write the
-  // ones tile of the row-sum MMA; the barrier orders the clearing before
-  // any thread's first P store.
+  // Clear P once (rows no unit writes must hold finite values); the barrier
+  // orders the clearing before any thread's first P store.
 #pragma unroll 1
   for (int i = tid; i < (int)(2 * kPBuf) / 16; i += kSoftmaxThreads)
     *reinterpret_cast<uint4*>(smem + kPOff + i * 16) = make_uint4(0, 0, 0, 0);
-#pragma unroll 1
-  for (int i = tid; i < 2048 / 16; i += kSoftmaxThreads)
-    *reinterpret_cast<uint4*>(smem + kOnesOff + i * 16) = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
   fence_proxy_async_smem();
   named_bar_sync(1, kSoftmaxThreads);
   PieceCursor cur;
@@ -995,6 +992,7 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
     if (tid == 0 && G < 100) NEB_TRACE_POINT(c, 1400 + G);
     const bool has_b = __any_sync(0xffffffffu, cr.jb >= 0);  // warp-uniform
     float m_a = neg_inf(), m_b = neg_inf();
+    float ls[2] = {0.f, 0.f};  // this thread's part of the row sums
     const int nst = stages_of(cr.lo, cr.hi);
     for (int s = 0; s < nst; ++s, ++G) {
       const int fs = G % kFlagSlots;
@@ -1033,7 +1031,10 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
       const int tok0 = t0 * kBlockTokens;
       float mxs[2];
       const bool blocks_ok = __all_sync(0xffffffffu, blk_ok == (1 << nblk) - 1);
-      const int lims[2] = {cr.len_a - tok0 - 2 * q4, cr.len_b - tok0 - 2 * q4};
+      // Columns past the row's length, or past the stage's nblk blocks (stale
+      // S of an earlier stage when a piece ends inside a row), are masked.
+      const int cols = nblk * kBlockTokens;
+      const int lims[2] = {min(cr.len_a - tok0, cols) - 2 * q4, min(cr.len_b - tok0, cols) - 2 * q4};
       if (has_b) {
         mask_max_rows<2>(sr, lims, blk_ok, blocks_ok, sc, mxs);
       } else {
@@ -1074,8 +1075,10 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
       uint8_t* pbuf = smem + kPOff + sb * kPBuf;
       const float ms[2] = {m_a, m_b};
       const int mrows[2] = {ma, mb};
-      if (has_b) store_p_rows<2>(sr, ms, mrows, pbuf, q4);
-      else store_p_rows<1>(sr, ms, mrows, pbuf, q4);
+      ls[0] *= alpha_a;
+      ls[1] *= alpha_b;
+      if (has_b) store_p_rows<2>(sr, ms, mrows, pbuf, q4, ls);
+      else store_p_rows<1>(sr, ms, mrows, pbuf, q4, ls);
       fence_proxy_async_smem();
       tc_fence_before();
       warp_arrive(&sh->p_full[sb]);
@@ -1083,7 +1086,7 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
       if (lane == 0 && G < 100) NEB_TRACE_POINT(c, 608 + 4 * G + (warp - kSoftmaxWarp0));
     }
     if (!ok) break;
-    if (!piece_epilogue(c, cr, G - 1, m_a, m_b, !have_next)) break;
+    if (!piece_epilogue(c, cr, G - 1, m_a, m_b, ls[0], ls[1], !have_next)) break;
     have = have_next;
     cr = nr;
   }
