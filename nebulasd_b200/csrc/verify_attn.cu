@@ -12,30 +12,29 @@
 //
 // One persistent CTA per SM (the driver places a single CTA that allocates
 // tensor memory on an SM); plan.cuh gives each an equal share of KV tiles.
-// The memory system runs saturated, so a global load on a critical path costs
-// microseconds: every role below waits only on its own inputs and every global
-// read it needs is issued well ahead.  K, S, softmax, P V and V of consecutive
-// 128-token stages overlap:
-//   warp 0      K producer: per 16-token KV block two 64-column TMA boxes
-//               (128-byte swizzle) into the K ring, once S of the stage that
-//               last used the slot is done; publishes the stage's block flags.
-//               Block-table rows are fetched two 32-tile batches ahead.
+// Work moves in 64-token stages (four 16-token blocks); K and V move by TMA in
+// ring slots of two stages (one transaction count and one wait per 32 KB).
+// The roles wait only on their own inputs:
+//   warp 0      K producer: per 16-token block two 64-column TMA boxes
+//               (128-byte swizzle), one lane per box, into the K ring, once S
+//               of the stages that last used the slot is done; publishes each
+//               stage's block flags.  Block-table rows are fetched two 32-tile
+//               batches ahead.
 //   warp 1      S issuer (one thread): Q of the next piece by TMA into the
-//               other half of a double buffer, S = Q K^T into a double-buffered
-//               TMEM tile (M=64, N=128).
-//   warps 2..5  softmax / epilogue: read S with tcgen05.ld, masked online
-//               softmax in the exp2 domain (O is rescaled only when a row's max
-//               grows by more than 2^8), P as fp16 in shared memory; at the end
-//               of a piece normalise O and store it, or store a partial.
+//               other half of a double buffer; S = Q K^T per stage into one of
+//               four TMEM tiles (M=64, N=64), so that it runs ahead of the
+//               softmax.
+//   warps 2..5  softmax / epilogue: read a stage's S with tcgen05.ld, masked
+//               online softmax in the exp2 domain (O is rescaled only when a
+//               row's max grows by more than 2^8), P as fp16 in shared memory,
+//               row sums of that P in fp32 registers; at the end of a piece
+//               normalise O and store it, or store or merge a partial.
 //   warp 6      V producer: the V boxes into the V ring, once P V of the
-//               stage that last used the slot is done.
+//               stages that last used the slot is done.
 //   warp 7      P V issuer (one thread): O += P V (V an MN-major operand) into
-//               a TMEM accumulator (M=64, N=128) and the row sums of P as
-//               P x ones (N=16).
-// Once the pipeline has drained, the whole CTA finishes the pieces of units
-// split across CTAs (at most two per CTA, its first and its last): it counts
-// each partial in and, in the CTA that completes the unit, merges the
-// partials by log-sum-exp.
+//               a TMEM accumulator (M=64, N=128).
+// A unit split across CTAs is merged by the CTA that finishes it last (see
+// piece_epilogue and finish_first_unit).
 //
 // Each role is an out-of-line function and the two producers share one, so
 // that the instruction cache holds every warp's hot loop at once: with more
