@@ -1,7 +1,7 @@
 """Benchmark of the paged verify-attention hot path (driver contract: one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload target_verify_8b|draft_decode_0p6b|long_verify_8b_k4|long_verify_8b_k8]
+                    [--workload target_verify_8b|draft_decode_0p6b|long_verify_8b_k4|long_verify_8b_k8|hostkv_copy]
                     [--kernel auto|decode|verify]
 
 Metric: paged verify-attention achieved HBM TB/s at the
@@ -21,6 +21,14 @@ at depth 4 with prefix lengths U[256, 4096].  Every step therefore streams
 Multi-GPU runs (torchrun) are weak scaling: each rank owns its own 16
 requests and pool, no collective on the path.  ``--impl reference`` times the
 reference semantics (the fp32 PyTorch-eager oracle) on the host cores.
+
+``--workload hostkv_copy`` measures the HostKV path instead: a step is one
+restore plan (host arena -> GPU cache, both planes) and one writeback plan
+(GPU -> host) of four requests' block runs, Qwen3-8B block size (36 layers,
+1,179,648 B per block and plane), through ``NativeCopyBackend`` in its kernel
+mode and in its copy-engine mode (one ``cudaMemcpyAsync`` per run and plane,
+the reference's transfer engine); ``value`` is its default (``auto``) mode; the
+roofline is a single large pinned copy measured in the same run.
 """
 from __future__ import annotations
 
@@ -356,9 +364,89 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_hostkv(args):
+    """HostKV restore/writeback bandwidth (rank 0 only; the copies are per GPU and PCIe-bound)."""
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    import numpy as np
+    from nebulasd_b200.hostkv import NativeCopyBackend
+    from tests.hostkv_support import Arena, CopyPlan, CopyRegion
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    layers, hk = 36, 8
+    gpu_blocks, host_blocks = 1280, 1024
+    shape = (gpu_blocks, layers, hk, 16, 128)
+    k_cache = torch.zeros(shape, dtype=torch.float16, device=dev)
+    v_cache = torch.zeros(shape, dtype=torch.float16, device=dev)
+    block_bytes = k_cache[0].numel() * 2
+    arena = Arena(host_blocks, block_bytes, "torch.float16", shape[1:])
+    rng = np.random.default_rng(1234)
+    arena.buf.fill(7)  # the bytes do not matter to a bit copy over PCIe
+    # Four requests' block runs (ctx U[1 K, 4 K] tokens): host extents and GPU
+    # ranges disjoint; at most 4 * 256 blocks, so GPU blocks 200.. stay below 1280.
+    counts = rng.integers(64, 257, 4).tolist()
+    host_off = np.cumsum([0] + counts[:-1]).tolist()
+    gpu_off = (np.cumsum([0] + counts[:-1]) + 200).tolist()
+    regions = tuple(CopyRegion(arena.make_extent(h, c), g, 0, c) for h, c, g in zip(host_off, counts, gpu_off))
+    moved = 2 * sum(counts) * block_bytes  # both planes
+    out = {}
+    for mode in ("auto", "kernel", "memcpy"):
+        be = NativeCopyBackend(arena=arena, k_cache=k_cache, v_cache=v_cache, mode=mode)
+        be.initialize()
+        res = {}
+        for direction in ("H2D", "D2H"):
+            plan = CopyPlan(direction, regions)
+            for _ in range(max(args.warmup, 3)):
+                be.launch(plan).synchronize()
+            ms = [0.0]
+            steps = max(1, min(args.steps, 20))
+            for _ in range(steps):
+                t = be.launch(plan)
+                t.synchronize()
+                ms.append(t.duration_ms())
+            res[direction] = moved * steps / (sum(ms) * 1e-3) / 1e9
+        be.close()
+        out[mode] = res
+    # Roofline: one contiguous pinned buffer of the same size through the copy engine.
+    host = torch.empty(moved // 2, dtype=torch.uint8, pin_memory=True)
+    devb = torch.empty(moved // 2, dtype=torch.uint8, device=dev)
+    peak = {}
+    for direction in ("H2D", "D2H"):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(4):
+            if i == 1:
+                e0.record()
+            if direction == "H2D":
+                devb.copy_(host, non_blocking=True)
+            else:
+                host.copy_(devb, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        peak[direction] = 3 * (moved // 2) / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    val = out["auto"]["H2D"]
+    line = {
+        "metric": "HostKV restore GB/s (both planes, Qwen3-8B blocks)", "value": round(val, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": max(1, min(args.steps, 20)), "warmup": max(args.warmup, 3),
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": "hostkv_copy", "requests": 4, "blocks": counts, "block_bytes": block_bytes,
+                   "bytes_per_plan": moved},
+        "writeback_gbs": round(out["auto"]["D2H"], 2),
+        "kernel_mode": {k: round(v, 2) for k, v in out["kernel"].items()},
+        "memcpy_mode": {k: round(v, 2) for k, v in out["memcpy"].items()},
+        "roofline": {"bound": "pcie", "achieved": round(val, 2), "peak": round(peak["H2D"], 2), "unit": "GB/s",
+                     "frac": round(val / peak["H2D"], 4), "peak_kind": "single pinned copy, same run",
+                     "peak_d2h": round(peak["D2H"], 2)},
+        "e2e": {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": moved, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
-    if args.impl == "reference":
+    if args.workload == "hostkv_copy":
+        run_hostkv(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -90,3 +90,20 @@ def test_op_modules_import_without_gpu():
     import nebulasd_b200
     from nebulasd_b200 import kernels, hostkv  # noqa: F401
     assert callable(kernels.paged_attention) and callable(nebulasd_b200.install)
+
+
+def test_copy_mode_choice_by_run_length():
+    """auto mode: copy engines for long runs, the single-launch kernel for many short ones."""
+    import numpy as np
+    from nebulasd_b200.hostkv import ENGINE_RUN_BYTES, choose_copy_mode, merged_runs
+    block = 1_179_648  # Qwen3-8B HostKV block (36 layers x 8 kv heads x 16 x 128 x 2 B)
+    long_runs = np.array([[0, 200, 253], [253, 453, 252]], dtype=np.int64)
+    assert merged_runs(long_runs) == 1  # adjacent on both sides: one run per plane
+    assert choose_copy_mode(long_runs, block, mapped=True) == "memcpy"
+    # 64 one-block regions, none adjacent: 64 driver calls per plane for 75 MB.
+    short = np.array([[2 * i, 3 * i, 1] for i in range(64)], dtype=np.int64)
+    assert merged_runs(short) == 64
+    assert choose_copy_mode(short, ENGINE_RUN_BYTES // 2, mapped=True) == "kernel"
+    assert choose_copy_mode(short, block, mapped=True) == "memcpy"  # 1.18 MB per run is long enough
+    assert choose_copy_mode(short, 4096, mapped=False) == "memcpy"  # unmapped arena: engines only
+    assert choose_copy_mode(np.zeros((0, 3), dtype=np.int64), block, mapped=True) == "kernel"
