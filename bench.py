@@ -1,7 +1,7 @@
 """Benchmark of the paged verify-attention hot path (driver contract: one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload target_verify_8b|draft_decode_0p6b|long_verify_8b_k4|long_verify_8b_k8|hostkv_copy]
+                    [--workload target_verify_8b|draft_decode_0p6b|long_verify_8b_k4|long_verify_8b_k8|hostkv_copy|kv_migrate]
                     [--kernel auto|decode|verify]
 
 Metric: paged verify-attention achieved HBM TB/s at the
@@ -29,6 +29,11 @@ restore plan (host arena -> GPU cache, both planes) and one writeback plan
 mode and in its copy-engine mode (one ``cudaMemcpyAsync`` per run and plane,
 the reference's transfer engine); ``value`` is its default (``auto``) mode; the
 roofline is a single large pinned copy measured in the same run.
+
+``--workload kv_migrate`` (two visible GPUs, one process) measures same-role
+migration: ``migrate_blocks`` copying four requests' block runs of Qwen3-8B
+blocks (both planes) from GPU 0's cache into GPU 1's over NVLink, in kernel
+mode (peer loads) and copy-engine mode, against a single large peer copy.
 """
 from __future__ import annotations
 
@@ -442,10 +447,79 @@ def run_hostkv(args):
     print(json.dumps(line), flush=True)
 
 
+def run_migrate(args):
+    """Same-role KV migration GPU 0 -> GPU 1 over NVLink (one process, two GPUs)."""
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    metric = "KV migration GB/s (NVLink peer, both planes, Qwen3-8B blocks)"
+    if torch.cuda.device_count() < 2:
+        print(json.dumps({"metric": metric, "unavailable": "needs two visible GPUs"}), flush=True)
+        return
+    import numpy as np
+    from nebulasd_b200.hostkv import migrate_blocks
+    src, dst = torch.device("cuda", 0), torch.device("cuda", 1)
+    shape = (1280, 36, 8, 16, 128)
+    sk = torch.full(shape, 1.0, dtype=torch.float16, device=src)
+    sv = torch.full(shape, 2.0, dtype=torch.float16, device=src)
+    dk = torch.zeros(shape, dtype=torch.float16, device=dst)
+    dv = torch.zeros(shape, dtype=torch.float16, device=dst)
+    block_bytes = sk[0].numel() * 2
+    rng = np.random.default_rng(1234)
+    counts = rng.integers(64, 257, 4).tolist()
+    soff = np.cumsum([0] + counts[:-1]).tolist()
+    doff = (np.cumsum([0] + counts[:-1]) + 200).tolist()  # at most 1024 + 200 < 1280 blocks
+    regions = [(a, b, c) for a, b, c in zip(soff, doff, counts)]
+    moved = 2 * sum(counts) * block_bytes
+    steps = max(1, min(args.steps, 20))
+    stream = torch.cuda.Stream(device=dst)
+    res = {}
+    for mode in ("kernel", "memcpy"):
+        for _ in range(max(args.warmup, 3)):
+            migrate_blocks(sk, sv, dk, dv, regions, mode=mode, stream=stream)
+        torch.cuda.synchronize(dst)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            migrate_blocks(sk, sv, dk, dv, regions, mode=mode, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize(dst)
+        res[mode] = moved * steps / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    # Roofline: one contiguous peer copy of one plane's bytes, on the same stream.
+    nbytes = moved // 2
+    a = sk.view(torch.uint8).reshape(-1)[:nbytes]
+    b = dk.view(torch.uint8).reshape(-1)[:nbytes]
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            b.copy_(a, non_blocking=True)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            b.copy_(a, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize(dst)
+    peak = 5 * nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    val = res["kernel"]
+    print(json.dumps({
+        "metric": metric, "value": round(val, 2), "unit": "GB/s", "n_gpus": 2, "steps": steps,
+        "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+        "dtype": "u8", "data": "synthetic",
+        "config": {"workload": "kv_migrate", "blocks": counts, "block_bytes": block_bytes, "bytes_per_step": moved},
+        "memcpy_mode": round(res["memcpy"], 2),
+        "roofline": {"bound": "nvlink", "achieved": round(val, 2), "peak": round(peak, 2), "unit": "GB/s",
+                     "frac": round(val / peak, 4), "peak_kind": "single peer copy, same run"},
+        "e2e": {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def main():
     args = _args()
     if args.workload == "hostkv_copy":
         run_hostkv(args)
+    elif args.workload == "kv_migrate":
+        run_migrate(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
