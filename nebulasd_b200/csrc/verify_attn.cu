@@ -83,6 +83,8 @@ constexpr long long kWaitLimit = 4000000000LL;
 constexpr int kMaxDirectOthers = 3;                      // direct merge: at most 3 other pieces
 constexpr int kPieceCost = 8;                             // a piece's fixed cost, in tiles (plan.cuh CostSplit)
 static_assert(kStageCols <= (int)kSBuf && kStageR % 2 == 0 && kSBufs * kSBuf <= kOCol, "S tiles fit TMEM");
+static_assert(kSlotStages == 2 && (kStageBlocks & (kStageBlocks - 1)) == 0 && 2 * kSlotStages * kStageBlocks <= 32,
+              "the producers fill a slot with two stages, one 64-column box per lane");
 
 // Shared memory map (offsets from a 1024-byte aligned base).
 constexpr uint32_t kQHalf = kMaxQRows * 128;       // one 64-column half of Q
