@@ -105,14 +105,20 @@ int neb_paged_attention_verify(const void* q, const void* k_cache, const void* v
  * streams, or an FFI host with no device allocator of its own.  This entry
  * takes the same arguments as neb_paged_attention_decode minus the workspace:
  * its split-K scratch is a 16 MiB static __device__ array inside this library
- * (held on every GPU that loads the library until the process exits).  Calls
- * needing more scratch than that (more SMs or a larger q/kv head ratio than a
- * B200 at ratio 8) fail with NEB_ERR_WORKSPACE.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) with that device
- * current, so make that first call before any stream capture.  Every call
- * clears the scratch it needs to start at zero, on `stream`, and allocates
- * nothing.  All calls share the one array: calls that may overlap on the GPU
- * (different streams without ordering between them) race and must not be made. */
+ * (held on every GPU that loads the library until the process exits).  A call
+ * uses as many split-K workers as the array holds partials for (on a B200 at
+ * q/kv head ratio 8, fewer than the workspace entry uses), so every ratio the
+ * decode kernel supports fits; a call that would still need more fails with
+ * NEB_ERR_WORKSPACE.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current and clears its
+ * header and counters, so make that first call before any stream capture.
+ * Every call clears the counters it needs to start at zero, on `stream`, and
+ * allocates nothing.  The error bits the kernel records (the bits of
+ * neb_workspace_status) accumulate in the array's header until
+ * neb_paged_attention_noalloc_status reads and clears them.  All calls share
+ * the one array: calls that may overlap on the GPU (different streams without
+ * ordering between them) race and must not be made.  The library keeps the
+ * array's address per device, so it must not outlive a reset of the device. */
 int neb_paged_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                        const int32_t* block_table, int32_t block_table_rows,
                                        int32_t max_blocks_per_seq, const int32_t* seq_lens,
@@ -121,9 +127,18 @@ int neb_paged_attention_decode_noalloc(const void* q, const void* k_cache, const
                                        int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
                                        float softmax_scale, void* o, void* stream);
 
+/* Status of the allocation-free entry on the current device: synchronises
+ * `stream`, then reads and clears the error bits its calls recorded since the
+ * last read (0 when no such call ran on the device).  Allocates nothing.  It
+ * has no counterpart in the reference (whose kernels record no errors). */
+int neb_paged_attention_noalloc_status(uint32_t* error_bits, void* stream);
+
 /* Synchronises `stream`, then reads the error bits the attention kernels
  * recorded in `workspace` (bit 0: block index out of range, bit 1: seq_id out
- * of range, bit 2: sequence longer than max_blocks_per_seq) and clears them. */
+ * of range, bit 2: sequence longer than max_blocks_per_seq, bit 3: a bounded
+ * wait gave up) and clears them.  After bit 3 it also clears the workspace's
+ * split-K arrival counters (the call that gave up left some of them counted),
+ * so call it before reusing a workspace whose last call may have failed. */
 int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream);
 
 /* ------------------------------------------------ QK-norm, RoPE and KV store

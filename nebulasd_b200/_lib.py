@@ -31,6 +31,7 @@ SIGNATURES = {
     "neb_paged_attention_decode": (_ATTN, ctypes.c_int),
     "neb_paged_attention_verify": (_ATTN, ctypes.c_int),
     "neb_paged_attention_decode_noalloc": (_ATTN[:18] + [_vp], ctypes.c_int),
+    "neb_paged_attention_noalloc_status": ([_u32p, _vp], ctypes.c_int),
     "neb_workspace_status": ([_vp, _u32p, _vp], ctypes.c_int),
     "neb_qk_norm_rope_store": ([_vp, _vp, _vp, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp,
                                 _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i64, _i32, _i32, _vp,

@@ -205,21 +205,37 @@ int neb_paged_attention_verify(const void* q, const void* k_cache, const void* v
                               softmax_scale, o, workspace, workspace_bytes, stream);
 }
 
-int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream) {
-  NEB_REQUIRE(workspace && error_bits, NEB_ERR_INVALID, "null argument");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+}  // extern "C"
+
+namespace neb {
+
+// Reads and clears the error bits of a workspace (or of the static scratch)
+// whose calls are ordered on `s`.  A call that gave up on a bounded wait
+// (kErrTimeout) stops without counting its split pieces in, so the arrival
+// counters it shared with other CTAs may be left above zero; they are cleared
+// here, before any later call can merge against them.
+static int read_and_clear_status(void* base, uint32_t* error_bits, cudaStream_t s) {
   WorkspaceHeader h;
-  NEB_CUDA(cudaMemcpyAsync(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost, s));
+  NEB_CUDA(cudaMemcpyAsync(&h, base, sizeof(h), cudaMemcpyDeviceToHost, s));
   NEB_CUDA(cudaStreamSynchronize(s));
   *error_bits = h.error_bits;
   if (h.error_bits) {
-    NEB_CUDA(cudaMemsetAsync(workspace, 0, sizeof(uint32_t), s));
+    NEB_CUDA(cudaMemsetAsync(base, 0, sizeof(uint32_t), s));
+    if (h.error_bits & kErrTimeout) {
+      const WorkspaceLayout L = workspace_layout(1, 1, 1, 1);
+      NEB_CUDA(cudaMemsetAsync(static_cast<char*>(base) + L.counters, 0, L.part_lse - L.counters, s));
+    }
     NEB_CUDA(cudaStreamSynchronize(s));
   }
   return NEB_OK;
 }
 
-}  // extern "C"
+}  // namespace neb
+
+extern "C" int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream) {
+  NEB_REQUIRE(workspace && error_bits, NEB_ERR_INVALID, "null argument");
+  return read_and_clear_status(workspace, error_bits, static_cast<cudaStream_t>(stream));
+}
 
 // ------------------------------------------------- allocation-free decode attention
 // For callers that cannot allocate device memory: the split-K scratch of the
@@ -230,8 +246,9 @@ int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream) {
 
 namespace neb {
 
-// Holds the header, the arrival counters and the partials of one decode call
-// on a B200 (148 SMs): at most about 11 MiB for q/kv head ratios up to 8.
+// Holds the header, the arrival counters and the partials of one decode call.
+// The call uses as many decode workers as fit (at most the workspace entry's
+// count), so every q/kv head ratio the decode kernel supports fits.
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -240,17 +257,31 @@ static void* g_noalloc_address[64] = {};
 
 // Device address of the static scratch on `device`, which must be current.
 // In host code `g_noalloc_scratch` names a host-side stand-in, not device
-// memory, so the address is looked up once per device and kept.
-static int noalloc_scratch_address(int device, void** address) {
+// memory, so the address is looked up once per device and kept (the library
+// must not outlive a reset of that device's context).  The first lookup also
+// clears the header and the counters on `s`.
+static int noalloc_scratch_address(int device, cudaStream_t s, void** address) {
   NEB_REQUIRE(device >= 0 && device < 64, NEB_ERR_UNSUPPORTED, "device index %d out of range", device);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   if (g_noalloc_address[device] == nullptr) {
     void* ptr = nullptr;
     NEB_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    const WorkspaceLayout L = workspace_layout(1, 1, 1, 1);
+    NEB_CUDA(cudaMemsetAsync(ptr, 0, L.part_lse, s));
     g_noalloc_address[device] = ptr;
   }
   *address = g_noalloc_address[device];
   return NEB_OK;
+}
+
+// Decode workers whose partials fit the static scratch next to its header and
+// counters (a multiple of the kernel's warps per CTA).
+static long long noalloc_workers(long long workers, int nq) {
+  const WorkspaceLayout L0 = workspace_layout(0, 1, 1, nq);
+  const size_t per_worker = (size_t)2 * nq * (kHeadDim + 1) * sizeof(float);
+  long long fit = (long long)((kNoAllocScratchBytes - L0.total - 512) / per_worker);
+  fit -= fit % 4;
+  return workers < fit ? workers : fit;
 }
 
 }  // namespace neb
@@ -272,20 +303,38 @@ extern "C" int neb_paged_attention_decode_noalloc(
   int nq = 0, group_rows = 0;
   rc = attention_workers(NEB_ATTN_DECODE, device, num_q_heads / num_kv_heads, &workers, &nq, &group_rows);
   if (rc != NEB_OK) return rc;
+  workers = noalloc_workers(workers, nq);
   const WorkspaceLayout L = workspace_layout(workers, num_rows, num_kv_heads, nq);
-  NEB_REQUIRE(L.total <= kNoAllocScratchBytes, NEB_ERR_WORKSPACE,
+  NEB_REQUIRE(workers >= 4 && L.total <= kNoAllocScratchBytes, NEB_ERR_WORKSPACE,
               "this call needs %zu bytes of scratch; the static scratch holds %zu", L.total,
               kNoAllocScratchBytes);
-  void* scratch = nullptr;
-  rc = noalloc_scratch_address(device, &scratch);
-  if (rc != NEB_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The array keeps the previous call's bytes.  The header and the counters
-  // this call can touch must start at zero; the partials are written before
-  // they are read.
-  NEB_CUDA(cudaMemsetAsync(scratch, 0, L.counters + (size_t)num_rows * num_kv_heads * sizeof(int32_t), s));
+  void* scratch = nullptr;
+  rc = noalloc_scratch_address(device, s, &scratch);
+  if (rc != NEB_OK) return rc;
+  // The array keeps the previous call's bytes.  The counters this call can
+  // touch must start at zero; the partials are written before they are read.
+  // The header's error bits are left to accumulate until
+  // neb_paged_attention_noalloc_status reads and clears them.
+  NEB_CUDA(cudaMemsetAsync(static_cast<char*>(scratch) + L.counters, 0,
+                           (size_t)num_rows * num_kv_heads * sizeof(int32_t), s));
   rc = bind_workspace(p, scratch, kNoAllocScratchBytes, workers, nq);
   if (rc != NEB_OK) return rc;
   p.max_group_rows = group_rows;
   return launch_decode(p, workers, s);
+}
+
+extern "C" int neb_paged_attention_noalloc_status(uint32_t* error_bits, void* stream) {
+  NEB_REQUIRE(error_bits, NEB_ERR_INVALID, "null argument");
+  int device = 0;
+  NEB_CUDA(cudaGetDevice(&device));
+  NEB_REQUIRE(device >= 0 && device < 64, NEB_ERR_UNSUPPORTED, "device index %d out of range", device);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    scratch = g_noalloc_address[device];
+  }
+  *error_bits = 0;
+  if (scratch == nullptr) return NEB_OK;  // no allocation-free call ran on this device
+  return read_and_clear_status(scratch, error_bits, static_cast<cudaStream_t>(stream));
 }

@@ -569,7 +569,10 @@ struct QFeeder {
       const int nrows = c.ps.gfirst[qg + 1] - first_row;
       const int rq = rows_per_quad(nrows);
       const int nquads = (nrows + rq - 1) / rq;
-      mbar_arrive_expect_tx(&sh->q_full[b], (uint32_t)nquads * 2u * 2048u);
+      // A box is gqa heads x 16 / gqa rows of 64 columns (fewer than 16 rows
+      // when gqa does not divide 16); rows past the tensor count as loaded.
+      const uint32_t box_bytes = (uint32_t)(c.gqa * (16 / c.gqa)) * 128u;
+      mbar_arrive_expect_tx(&sh->q_full[b], (uint32_t)nquads * 2u * box_bytes);
 #pragma unroll 1
       for (int q = 0; q < nquads; ++q)
         for (int dh = 0; dh < 2; ++dh)
@@ -1209,9 +1212,15 @@ long long verify_workers(int device) { return num_sms(device); }
 
 int verify_max_rows() { return kVerifyMaxRows; }
 
+// Rows of one request per unit.  A unit's rows are cut into four chunks of
+// ceil(rows / 4) rows; a chunk's gqa * ceil(rows / 4) query rows must fit the
+// 16 lanes of one TMEM quadrant (one softmax warp) and the 16 / gqa rows of
+// one Q box, so at most 4 * floor(16 / gqa) rows (64 / gqa rounded down to a
+// multiple of 4 rows per chunk: 20 rather than 21 at gqa 3, 4 rather than 7
+// at gqa 9).
 int verify_group_rows(int gqa) {
   if (gqa < 1 || gqa > kMaxGqa) return 0;
-  return kMaxQRows / gqa;
+  return 4 * (16 / gqa);
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1289,8 +1298,8 @@ int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream) {
               "KV cache of %llu rows exceeds the verify kernel's 2^31-row tensor map", rows);
   NEB_REQUIRE(p.num_rows <= kVerifyMaxRows, NEB_ERR_UNSUPPORTED,
               "verify attention takes at most %d rows per call (got %d)", kVerifyMaxRows, p.num_rows);
-  NEB_REQUIRE(gqa >= 1 && gqa <= kMaxGqa && p.max_group_rows * gqa <= kMaxQRows, NEB_ERR_INVALID,
-              "group rows exceed the MMA tile");
+  NEB_REQUIRE(gqa >= 1 && gqa <= kMaxGqa && p.max_group_rows >= 1 && p.max_group_rows <= verify_group_rows(gqa),
+              NEB_ERR_INVALID, "group rows exceed what one TMEM quadrant per chunk holds");
   NEB_REQUIRE((reinterpret_cast<uintptr_t>(p.q) & 15u) == 0, NEB_ERR_INVALID, "q must be 16-byte aligned");
   CUtensorMap tk, tv, tq;
   {

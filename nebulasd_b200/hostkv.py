@@ -229,12 +229,18 @@ class _PoolAdapter:
 
 
 def migrate_blocks(src_k: torch.Tensor, src_v: torch.Tensor, dst_k: torch.Tensor, dst_v: torch.Tensor,
-                   regions, *, mode: str = "kernel", stream: torch.cuda.Stream | None = None) -> None:
+                   regions, *, mode: str = "kernel", stream: torch.cuda.Stream | None = None,
+                   src_stream: torch.cuda.Stream | None = None) -> None:
     """Copy ``(src_block, dst_block, count)`` block ranges from one GPU's caches to another's.
 
-    Runs on ``dst``'s device.  ``mode="kernel"`` reads the source cache over
-    NVLink from a copy kernel (peer access is enabled on first use);
-    ``mode="memcpy"`` issues peer ``cudaMemcpyAsync`` per merged run.
+    Runs on ``dst``'s device, on ``stream`` (default: its current stream).
+    ``mode="kernel"`` reads the source cache over NVLink from a copy kernel
+    (peer access is enabled on first use); ``mode="memcpy"`` issues peer
+    ``cudaMemcpyAsync`` per merged run.  The copy is ordered after the work
+    queued so far on ``src_stream`` (default: the source device's current
+    stream), where the caller wrote the source KV, through an event the copy's
+    stream waits on; the caller keeps the source blocks unchanged until the
+    copy is done (``stream`` synchronised or waited on).
     """
     if src_k.shape[1:] != dst_k.shape[1:] or src_k.dtype != dst_k.dtype:
         raise ValueError("source and destination caches must share the block layout")
@@ -242,10 +248,14 @@ def migrate_blocks(src_k: torch.Tensor, src_v: torch.Tensor, dst_k: torch.Tensor
     if len(arr) and ((arr[:, 0] + arr[:, 2]).max() > src_k.shape[0] or (arr[:, 1] + arr[:, 2]).max() > dst_k.shape[0]):
         raise ValueError("migration range exceeds a KV cache")
     block_bytes = src_k[0].numel() * src_k.element_size()
+    src_s = src_stream or torch.cuda.current_stream(src_k.device)
+    ready = torch.cuda.Event()
+    ready.record(src_s)
     with torch.cuda.device(dst_k.device):
         if src_k.device != dst_k.device:
             _lib.check(_lib.lib.neb_enable_peer_access(src_k.device.index), "neb_enable_peer_access")
         s = stream or torch.cuda.current_stream(dst_k.device)
+        s.wait_event(ready)
         rc = _lib.lib.neb_kv_peer_copy(src_k.data_ptr(), src_v.data_ptr(), dst_k.data_ptr(), dst_v.data_ptr(),
                                        block_bytes, arr.ctypes.data, len(arr), MODES[mode], s.cuda_stream)
         _lib.check(rc, "neb_kv_peer_copy")

@@ -42,14 +42,21 @@ def get_kernel() -> str:
 VERIFY_BUILT = os.environ.get("NEB_VERIFY_BUILT", "1") == "1"
 
 
+DECODE_RATIOS = (1, 2, 4, 8)  # q/kv head ratios the CUDA-core kernel is built for
+
+
 def choose_kernel(num_q_heads: int, num_kv_heads: int, num_rows: int = 0) -> int:
     """Tensor-core kernel for GQA ratios 4..16 (the rows x heads of a request
-    fill its MMA tiles) up to its row limit; the CUDA-core kernel otherwise."""
+    fill its MMA tiles) and for every ratio the CUDA-core kernel is not built
+    for (3, 5, 6, 7, 9..16), up to its row limit; the CUDA-core kernel for
+    ratios 1 and 2 and for batches beyond that limit."""
     forced = _MODES[_mode]
     if forced is not None:
         return forced
     gqa = num_q_heads // num_kv_heads
-    if VERIFY_BUILT and 4 <= gqa <= 16 and num_rows <= _lib.lib.neb_attention_max_rows(_lib.NEB_ATTN_VERIFY):
+    fits_verify = VERIFY_BUILT and 1 <= gqa <= 16 and \
+        num_rows <= _lib.lib.neb_attention_max_rows(_lib.NEB_ATTN_VERIFY)
+    if fits_verify and (gqa >= 4 or gqa not in DECODE_RATIOS):
         return _lib.NEB_ATTN_VERIFY
     return _lib.NEB_ATTN_DECODE
 

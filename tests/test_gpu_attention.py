@@ -90,6 +90,64 @@ def test_random_batches_match_oracle(kernel, shape, seed, cuda):
     torch.testing.assert_close(run_attention(c, kernel, cuda), oracle_of(c), atol=ATOL, rtol=RTOL)
 
 
+# Every q/kv head ratio the verify kernel accepts that the decode kernel is not
+# built for, or whose unit rows do not fill whole 16-lane chunks, at depths 4
+# and 8: a unit's rows are cut into four chunks of gqa * ceil(rows / 4) query
+# rows, which must each fit one TMEM lane quadrant.  Depth 20 at gqa 3 gives a
+# request of 21 rows, one more than a unit holds.
+GQA_SHAPES = {
+    f"gqa{g}_k{k}": dict(num_requests=5, depth=k, ctx_lo=10, ctx_hi=700, num_q_heads=2 * g, num_kv_heads=2,
+                         pool_blocks=300)
+    for g in (3, 5, 6, 7, 9, 12, 16) for k in (4, 8)
+}
+GQA_SHAPES["gqa3_k20"] = dict(num_requests=3, depth=20, ctx_lo=30, ctx_hi=500, num_q_heads=6, num_kv_heads=2,
+                              pool_blocks=120)
+GQA_SHAPES["gqa5_ragged"] = dict(num_requests=6, depth=[8, 0, 3, 11, 1, 5], ctx_lo=1, ctx_hi=600,
+                                 num_q_heads=10, num_kv_heads=2, pool_blocks=300, shuffle_seq_ids=True)
+
+
+@pytest.mark.skipif(not VERIFY_BUILT, reason="verify kernel not built")
+@pytest.mark.parametrize("shape", sorted(GQA_SHAPES))
+def test_verify_every_gqa_ratio_matches_oracle(shape, cuda):
+    c = batch_case(3000 + sorted(GQA_SHAPES).index(shape), **GQA_SHAPES[shape])
+    torch.testing.assert_close(run_attention(c, "verify", cuda), oracle_of(c), atol=ATOL, rtol=RTOL)
+
+
+def test_auto_dispatch_serves_every_ratio_up_to_16(cuda):
+    """The drop-in entry picks a kernel for every integer q/kv head ratio 1..16, as the reference accepts."""
+    from nebulasd_b200.kernels import paged_attention_raw
+    for g in range(1, 17):
+        c = batch_case(4000 + g, num_requests=3, depth=4, ctx_lo=20, ctx_hi=300, num_q_heads=g, num_kv_heads=1,
+                       pool_blocks=80)
+        q = c["q"].to(cuda)
+        o = torch.empty_like(q)
+        paged_attention_raw(q, c["k_cache"].to(cuda), c["v_cache"].to(cuda), c["block_table"].to(cuda),
+                            c["seq_lens"].to(cuda), c["seq_ids"].to(cuda), c["cur_layer"], c["softmax_scale"], o)
+        torch.cuda.synchronize(cuda)
+        torch.testing.assert_close(o.float().cpu(), oracle_of(c), atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_status_after_timeout_clears_stale_counters(kernel, cuda):
+    """A call that gave up on a bounded wait leaves split counters counted; the status call clears them.
+
+    The failed call is stood in for on the host: the timeout bit and non-zero
+    counters are written into the workspace, as such a call leaves them.
+    """
+    from nebulasd_b200._workspace import attention_workspace, workspace_errors
+    stream = torch.cuda.current_stream(cuda)
+    ws = attention_workspace(_kernel_id(kernel), cuda, stream, 4096, 32, 8)
+    counters = ws[256:256 + 4096 * 64 * 4].view(torch.int32)
+    header = ws[:4].view(torch.int32)
+    header.fill_(8)                 # kErrTimeout
+    counters[:4096].fill_(1)        # pieces counted in by the CTAs that did not give up
+    assert workspace_errors(ws, stream) == 8
+    assert int(torch.count_nonzero(counters).item()) == 0
+    assert workspace_errors(ws, stream) == 0
+    c = batch_case(61, **SHAPES["one_unit_all_ctas"])
+    torch.testing.assert_close(run_attention(c, kernel, cuda, workspace=ws), oracle_of(c), atol=ATOL, rtol=RTOL)
+
+
 @pytest.mark.parametrize("kernel", KERNELS)
 def test_zero_length_rows_give_nan_and_others_unaffected(kernel, cuda):
     c = dict(C.attention_cases()["decode_edges"])
