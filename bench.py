@@ -64,7 +64,7 @@ def _args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--workload", default="target_verify_8b")
-    ap.add_argument("--kernel", default="auto", choices=("auto", "decode", "verify"))
+    ap.add_argument("--kernel", default="auto", choices=("auto", "decode", "verify", "verify_long"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--layers", type=int, default=None,
@@ -194,8 +194,9 @@ def run_ours(args):
     set_kernel(args.kernel)
 
     b, layers, cfg = build_workload(args.workload, 1234 + 7919 * rank, dev, args.layers)
-    kernel = choose_kernel(b.num_q_heads, b.num_kv_heads, int(b.q.shape[0]))
-    kname = "verify" if kernel == _lib.NEB_ATTN_VERIFY else "decode"
+    kernel = choose_kernel(b.num_q_heads, b.num_kv_heads, int(b.q.shape[0]), max(b.seq_lens_list))
+    kname = {_lib.NEB_ATTN_DECODE: "decode", _lib.NEB_ATTN_VERIFY: "verify",
+             _lib.NEB_ATTN_VERIFY_LONG: "verify_long"}[kernel]
     o = torch.empty_like(b.q)
     stream = torch.cuda.current_stream(dev)
     scale = b.q.shape[-1] ** -0.5

@@ -62,8 +62,9 @@ const char* neb_last_error(void);
  * (phase 1 :9-108, phase 2 :111-149), whose fp32 mid_o / mid_o_logexpsum
  * buffers (:170-180) this workspace stands in for.
  */
-#define NEB_ATTN_DECODE 0  /* CUDA-core kernel: 128-bit loads, warp shuffles */
-#define NEB_ATTN_VERIFY 1  /* tcgen05 kernel: GQA x rows packed into MMA tiles */
+#define NEB_ATTN_DECODE 0       /* CUDA-core kernel: 128-bit loads, warp shuffles */
+#define NEB_ATTN_VERIFY 1       /* tcgen05 kernel: GQA x rows packed into MMA tiles */
+#define NEB_ATTN_VERIFY_LONG 2  /* tcgen05 kernel for long prefixes: KV tokens on the MMA's M */
 
 size_t neb_attention_workspace_bytes(int kernel, int device, int num_rows, int num_q_heads,
                                      int num_kv_heads);
@@ -132,6 +133,25 @@ int neb_paged_attention_decode_noalloc(const void* q, const void* k_cache, const
  * last read (0 when no such call ran on the device).  Allocates nothing.  It
  * has no counterpart in the reference (whose kernels record no errors). */
 int neb_paged_attention_noalloc_status(uint32_t* error_bits, void* stream);
+
+/* Target verify attention for long prefixes (thousands of tokens per request
+ * and kv head), on tcgen05 tensor cores in the other orientation: 128 KV
+ * tokens are the M dimension of S^T = K Q^T and of O^T += V^T P^T, and the GQA
+ * heads x adjacent rows of one request (up to 64 query columns) the N
+ * dimension, so that a 64 KB stage of K and V costs eight MMAs per issuing
+ * thread.  Faster than neb_paged_attention_verify once the steady state
+ * dominates (prefixes of about 8 K tokens and more); slower for short ones,
+ * whose fixed per-launch costs it does not reduce.  Same arguments, semantics
+ * and workspace contract as the decode entry; q/kv head ratios 1..64.
+ * Replaces the same reference function: paged_attn.py:152-222. */
+int neb_paged_attention_verify_long(const void* q, const void* k_cache, const void* v_cache,
+                                    const int32_t* block_table, int32_t block_table_rows,
+                                    int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                                    const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                                    int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                    int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                                    float softmax_scale, void* o, void* workspace,
+                                    size_t workspace_bytes, void* stream);
 
 /* Synchronises `stream`, then reads the error bits the attention kernels
  * recorded in `workspace` (bit 0: block index out of range, bit 1: seq_id out

@@ -30,6 +30,7 @@ SIGNATURES = {
     "neb_attention_max_rows": ([ctypes.c_int], ctypes.c_int),
     "neb_paged_attention_decode": (_ATTN, ctypes.c_int),
     "neb_paged_attention_verify": (_ATTN, ctypes.c_int),
+    "neb_paged_attention_verify_long": (_ATTN, ctypes.c_int),
     "neb_paged_attention_decode_noalloc": (_ATTN[:18] + [_vp], ctypes.c_int),
     "neb_paged_attention_noalloc_status": ([_u32p, _vp], ctypes.c_int),
     "neb_workspace_status": ([_vp, _u32p, _vp], ctypes.c_int),
@@ -53,6 +54,7 @@ for _name, (_args, _res) in SIGNATURES.items():
 
 NEB_ATTN_DECODE = 0
 NEB_ATTN_VERIFY = 1
+NEB_ATTN_VERIFY_LONG = 2
 
 
 class NebError(RuntimeError):

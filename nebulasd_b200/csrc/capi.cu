@@ -37,6 +37,12 @@ long long verify_workers(int device);
 int verify_group_rows(int gqa);
 int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream);
 int verify_max_rows();
+namespace vlong {
+long long verify_workers(int device);
+int verify_group_rows(int gqa);
+int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream);
+int verify_max_rows();
+}  // namespace vlong
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
@@ -115,6 +121,11 @@ static int attention_workers(int kernel, int device, int gqa, long long* workers
     NEB_REQUIRE(*group_rows > 0, NEB_ERR_UNSUPPORTED,
                 "verify attention supports q/kv head ratios 1..16 (got %d)", gqa);
     *workers = verify_workers(device);
+  } else if (kernel == NEB_ATTN_VERIFY_LONG) {
+    *group_rows = vlong::verify_group_rows(gqa);
+    NEB_REQUIRE(*group_rows > 0, NEB_ERR_UNSUPPORTED,
+                "long-context verify attention supports q/kv head ratios 1..64 (got %d)", gqa);
+    *workers = vlong::verify_workers(device);
   } else {
     return set_error(NEB_ERR_INVALID, "unknown attention kernel %d", kernel);
   }
@@ -135,6 +146,7 @@ const char* neb_last_error(void) { return g_last_error; }
 
 int neb_attention_max_rows(int kernel) {
   if (kernel == NEB_ATTN_VERIFY) return verify_max_rows();
+  if (kernel == NEB_ATTN_VERIFY_LONG) return vlong::verify_max_rows();
   return kernel == NEB_ATTN_DECODE ? kMaxRows : 0;
 }
 
@@ -174,7 +186,8 @@ static int paged_attention_impl(int kernel, const void* q, const void* k_cache, 
   if (rc != NEB_OK) return rc;
   p.max_group_rows = group_rows;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return kernel == NEB_ATTN_DECODE ? launch_decode(p, workers, s) : launch_verify(p, workers, s);
+  if (kernel == NEB_ATTN_DECODE) return launch_decode(p, workers, s);
+  return kernel == NEB_ATTN_VERIFY ? launch_verify(p, workers, s) : vlong::launch_verify(p, workers, s);
 }
 
 int neb_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache,
@@ -200,6 +213,20 @@ int neb_paged_attention_verify(const void* q, const void* k_cache, const void* v
                                float softmax_scale, void* o, void* workspace,
                                size_t workspace_bytes, void* stream) {
   return paged_attention_impl(NEB_ATTN_VERIFY, q, k_cache, v_cache, block_table, block_table_rows,
+                              max_blocks_per_seq, seq_lens, seq_ids, num_rows, num_q_heads,
+                              num_kv_heads, head_dim, block_size, num_blocks, num_layers, cur_layer,
+                              softmax_scale, o, workspace, workspace_bytes, stream);
+}
+
+int neb_paged_attention_verify_long(const void* q, const void* k_cache, const void* v_cache,
+                                    const int32_t* block_table, int32_t block_table_rows,
+                                    int32_t max_blocks_per_seq, const int32_t* seq_lens,
+                                    const int32_t* seq_ids, int32_t num_rows, int32_t num_q_heads,
+                                    int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                    int64_t num_blocks, int32_t num_layers, int32_t cur_layer,
+                                    float softmax_scale, void* o, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  return paged_attention_impl(NEB_ATTN_VERIFY_LONG, q, k_cache, v_cache, block_table, block_table_rows,
                               max_blocks_per_seq, seq_lens, seq_ids, num_rows, num_q_heads,
                               num_kv_heads, head_dim, block_size, num_blocks, num_layers, cur_layer,
                               softmax_scale, o, workspace, workspace_bytes, stream);

@@ -47,7 +47,11 @@
 //
 // Every wait is bounded (about 2 s); on expiry the kernel records an error
 // bit, stops issuing work, waits (bounded) for its own copies and MMAs, frees
-// its TMEM and returns.  No TMA multicast is used.
+// its TMEM and returns.  No TMA multicast is used.  The kernel is launched
+// with programmatic stream serialisation: it lets the next launch in the
+// stream be scheduled as soon as it starts, and waits (griddepcontrol.wait)
+// for the previous one before it reads any input, so that the launch gap and
+// the previous launch's tail overlap.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -119,7 +123,6 @@ struct Ctx {
   long long total, workers, w, t_begin, t_end;
   CostSplit split;  // which worker owns which tiles
   uint32_t tmem;
-  unsigned long long* trace;  // timeline buffer row of this CTA (builds with NEB_TRACE only)
 };
 
 struct VerifyShared {
@@ -156,47 +159,6 @@ struct VerifyArgs {
   int oob_row;  // first row past the end of the K/V tensor maps (loads there return zeros)
 };
 
-// Timeline hooks: empty unless the library is built with -DNEB_TRACE, in which
-// case each CTA stamps %globaltimer into a caller-provided buffer (offline
-// profiling of the pipeline; the shipped build contains no tracing code).
-#ifdef NEB_TRACE
-__device__ unsigned long long* g_trace = nullptr;
-#define NEB_TRACE_POINT(c, i)                                \
-  do {                                                       \
-    if ((c).trace) {                                         \
-      unsigned long long t_;                                 \
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); \
-      (c).trace[(i)] = t_;                                   \
-    }                                                        \
-  } while (0)
-#define NEB_PHASE_DECL() long long neb_ph[4] = {0, 0, 0, 0}, neb_t = clock64()
-#define NEB_PHASE(k)                 \
-  do {                               \
-    const long long t2_ = clock64(); \
-    neb_ph[(k)] += t2_ - neb_t;      \
-    neb_t = t2_;                     \
-  } while (0)
-#define NEB_PHASE_DUMP(c, n)                                                   \
-  do {                                                                         \
-    if ((c).trace && threadIdx.x == kSoftmaxWarp0 * 32) {                      \
-      for (int k_ = 0; k_ < 4; ++k_) (c).trace[2000 + k_] = neb_ph[k_];        \
-      (c).trace[2004] = (n);                                                   \
-    }                                                                          \
-  } while (0)
-#else
-#define NEB_TRACE_POINT(c, i) \
-  do {                        \
-  } while (0)
-#define NEB_PHASE_DECL() \
-  do {                   \
-  } while (0)
-#define NEB_PHASE(k) \
-  do {               \
-  } while (0)
-#define NEB_PHASE_DUMP(c, n) \
-  do {                       \
-  } while (0)
-#endif
 
 // The pieces of one worker: a cursor over its tile range (plan.cuh).
 struct PieceCursor {
@@ -425,7 +387,6 @@ struct FirstSplit {
       c.sh->first_last = 1;
     }
     pending = false;
-    NEB_TRACE_POINT(c, 1997);
   }
 };
 
@@ -484,13 +445,8 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
     feed.get_lane(pos, (st ? n0 : 0) + b, row, valid);
     int waited = 1;
     if (lane == 0) {
-      if (G < 90) NEB_TRACE_POINT(c, (flags ? 1010 : 1110) + G);
       waited = wait_or_abort(sh, p, &empty[slot], phase ^ 1u);
       if (waited) {
-        if (G < 99) {
-          NEB_TRACE_POINT(c, (flags ? 8 : 508) + G);
-          NEB_TRACE_POINT(c, (flags ? 8 : 508) + G + 1);
-        }
         mbar_arrive_expect_tx(&full[slot], (uint32_t)(n0 + n1) * 2u * 2048u);
       }
     }
@@ -610,13 +566,11 @@ __device__ __noinline__ void s_issuer(const Ctx& c, const CUtensorMap* tmap_q) {
     const uint32_t qb = q_base + b * kQBuf;
     for (int s = 0; s < nst; ++s, ++G) {
       const int slot = (G / kSlotStages) % kKRing, sb = G % kSBufs;
-      if (G < 90) NEB_TRACE_POINT(c, 1210 + G);
       if (!wait_or_abort(sh, p, &sh->k_full[slot], (uint32_t)((G / kSlotStages / kKRing) & 1)) ||
           !wait_or_abort(sh, p, &sh->s_empty[sb], (uint32_t)(((G / kSBufs) & 1) ^ 1))) {
         ok = false;
         break;
       }
-      if (G < 100) NEB_TRACE_POINT(c, 108 + G);
       tc_fence_after();
       const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
       const uint32_t idesc_s = idesc_f16_f32(kMaxQRows, 16 * nblk, false, false);
@@ -663,14 +617,12 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
     const int nst = stages_of(lo, hi);
     for (int s = 0; s < nst; ++s, ++G) {
       const int slot = (G / kSlotStages) % kVRing, sb = G & 1;
-      if (G < 90) NEB_TRACE_POINT(c, 1310 + G);
       if (!wait_or_abort(sh, p, &sh->p_full[sb], (uint32_t)((G >> 1) & 1)) ||
           !wait_or_abort(sh, p, &sh->v_full[slot], (uint32_t)((G / kSlotStages / kVRing) & 1)) ||
           (s == 0 && piece > 0 && !wait_or_abort(sh, p, &sh->o_empty, (uint32_t)((piece - 1) & 1)))) {
         ok = false;
         break;
       }
-      if (G < 100) NEB_TRACE_POINT(c, 208 + G);
       tc_fence_after();
       const int nblk = min(kStageBlocks, hi - (lo + s * kStageBlocks));
       const uint32_t vst = v_base + slot * kSlotBytes + (G % kSlotStages) * kStageBytes;
@@ -744,19 +696,15 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
       if (tid == 0) sh->merge_mode = ld_acquire_gpu(p.counters + unit) == (int)(w1 - w0);
       named_bar_sync(2, kSoftmaxThreads);
       direct = sh->merge_mode != 0;
-      if (tid == 0) NEB_TRACE_POINT(c, 1990);
-      if (tid == 0 && c.trace) c.trace[1995] = direct ? 1 : 2;
     }
   }
   if (!wait_or_abort(sh, p, &sh->pv_done[G_last & 1], (uint32_t)((G_last >> 1) & 1))) return false;
-  if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1508 + G_last);
   tc_fence_after();
   // Row sums: each of a row's four threads holds the sum of its columns.
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-  if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1900 + G_last);
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     uint32_t o[32];
@@ -843,7 +791,6 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
       swap_rows_n<8>(o);  // row b's values into row a's registers
     }
   }
-  if (tid == 0 && last_piece) NEB_TRACE_POINT(c, 1991);
   if (!whole) {
     if (direct) {
       if (tid == 0) p.counters[unit] = 0;  // the unit is complete: ready for the next call
@@ -856,8 +803,6 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
         const int last = atomicAdd(p.counters + unit, 1) == (int)(w1 - w0);
         if (last) p.counters[unit] = 0;
         sh->merge_mode = last;
-        NEB_TRACE_POINT(c, 1992);
-        if (c.trace) c.trace[1996] = last ? 3 : 4;
       }
       named_bar_sync(2, kSoftmaxThreads);
       if (sh->merge_mode) {
@@ -866,7 +811,6 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
       }
     }
   }
-  if (threadIdx.x == kSoftmaxWarp0 * 32 && G_last < 100) NEB_TRACE_POINT(c, 1800 + G_last);
   return true;
 }
 
@@ -990,10 +934,8 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
   bool have = fill(cr);
   int G = 0;
   bool ok = true;
-  NEB_PHASE_DECL();
   while (have && ok) {
     const bool have_next = fill(nr);
-    if (tid == 0 && G < 100) NEB_TRACE_POINT(c, 1400 + G);
     const bool has_b = __any_sync(0xffffffffu, cr.jb >= 0);  // warp-uniform
     float m_a = neg_inf(), m_b = neg_inf();
     float ls[2] = {0.f, 0.f};  // this thread's part of the row sums
@@ -1007,8 +949,6 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
         ok = false;
         break;
       }
-      if (tid == 0 && G < 100) NEB_TRACE_POINT(c, 308 + G);
-      NEB_PHASE(0);
       tc_fence_after();
       uint32_t sr[4 * kStageR];
       {
@@ -1029,7 +969,6 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
       tmem_wait_ld();
       tc_fence_before();
       warp_arrive(&sh->s_empty[sbuf]);
-      NEB_PHASE(1);
       const int t0 = cr.lo + s * kStageBlocks;
       const int nblk = min(kStageBlocks, cr.hi - t0);
       const int tok0 = t0 * kBlockTokens;
@@ -1062,7 +1001,6 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
           m_b = mxb;
         }
       }
-      NEB_PHASE(2);
       // P buffer sb is free once PV(G-2) completed.
       if (G >= 2 && !wait_or_abort(sh, p, &sh->pv_done[sb], (uint32_t)(((G - 2) >> 1) & 1))) {
         ok = false;
@@ -1086,15 +1024,12 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
       fence_proxy_async_smem();
       tc_fence_before();
       warp_arrive(&sh->p_full[sb]);
-      NEB_PHASE(3);
-      if (lane == 0 && G < 100) NEB_TRACE_POINT(c, 608 + 4 * G + (warp - kSoftmaxWarp0));
     }
     if (!ok) break;
     if (!piece_epilogue(c, cr, G - 1, m_a, m_b, ls[0], ls[1], !have_next)) break;
     have = have_next;
     cr = nr;
   }
-  NEB_PHASE_DUMP(c, G);
 }
 
 __global__ void __launch_bounds__(kVThreads, 1)
@@ -1111,17 +1046,13 @@ __global__ void __launch_bounds__(kVThreads, 1)
   c.p = &p;
   c.sh = sh;
   c.smem = smem;
-  c.trace = nullptr;
-#ifdef NEB_TRACE
-  if (g_trace) c.trace = g_trace + blockIdx.x * 2048;
-#endif
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 0);
+  grid_launch_dependents();
+  grid_dependency_wait();  // inputs may come from the previous launch in the stream
   c.ps = PlanSmem{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1),
                   plan_mem + 2 * (p.num_rows + 1) + 8};
   build_plan(c.ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, p.max_group_rows);
   c.ng = c.ps.misc[0];
-  if (threadIdx.x == 0) NEB_TRACE_POINT(c, 1);
   c.hk = p.num_kv_heads;
   c.gqa = p.num_q_heads / p.num_kv_heads;
   c.oob_row = args.oob_row;
@@ -1183,7 +1114,6 @@ __global__ void __launch_bounds__(kVThreads, 1)
   if (threadIdx.x == 0) sh->ctx.tmem = sh->tmem_base;
   __syncthreads();
   const Ctx& cs = sh->ctx;
-  if (threadIdx.x == 0) NEB_TRACE_POINT(cs, 2);
 
   if (warp == kKWarp) {
     FirstSplit first;
@@ -1197,14 +1127,12 @@ __global__ void __launch_bounds__(kVThreads, 1)
     if (lane == 0) pv_issuer(cs);
   } else {
     softmax_role(cs);
-    if (warp == kSoftmaxWarp0 && lane == 0) NEB_TRACE_POINT(cs, 3);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == kSWarp) tmem_dealloc(cs.tmem, kTmemCols);
   if (!aborted(sh) && sh->first_last) finish_first_unit(cs);
-  if (threadIdx.x == 0) NEB_TRACE_POINT(cs, 4);
 }
 
 // ------------------------------------------------------------------ host side
@@ -1335,8 +1263,17 @@ int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream) {
       attr_set[device] = true;
     }
   }
-  verify_attn_kernel<<<(unsigned)workers, kVThreads, smem, stream>>>(tk, tv, tq, a);
-  NEB_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)workers);
+  cfg.blockDim = dim3(kVThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  NEB_CUDA(cudaLaunchKernelEx(&cfg, verify_attn_kernel, tk, tv, tq, a));
   return NEB_OK;
 }
 

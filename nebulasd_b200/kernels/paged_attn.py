@@ -4,13 +4,18 @@ Replaces ``swiftLLM/swiftllm/worker/kernels/paged_attn.py:152-222``.  Same
 arguments, same contiguity assertions (``:163-168``), same outputs written into
 ``o``; one launch instead of two, no per-call ``torch.empty`` of partials.
 
-Two CUDA kernels implement it (both correct for any row layout):
+Three CUDA kernels implement it (all correct for any row layout):
   * ``decode``: CUDA cores, for the Draft's single-token rows;
   * ``verify``: tcgen05 tensor cores, packing the GQA group and the k+1
-    speculative rows of one request into the M dimension of the MMA tile.
-``NEB_PAGED_ATTENTION=decode|verify|auto`` (or ``set_kernel``) picks one; ``auto``
-uses ``verify`` when the q/kv head ratio is 4 or more (the Qwen3-8B Target)
-and ``decode`` otherwise (the Qwen3-0.6B Draft), when both are built.
+    speculative rows of one request into the M dimension of the MMA tile;
+  * ``verify_long``: tcgen05 tensor cores with 128 KV tokens on the M
+    dimension, for long prefixes (the steady state dominates there).
+``NEB_PAGED_ATTENTION=decode|verify|verify_long|auto`` (or ``set_kernel``)
+picks one; ``auto`` uses a verify kernel when the q/kv head ratio is 4 or more
+(the Qwen3-8B Target) or not one the decode kernel is built for, the long
+variant when the batch's longest row has ``LONG_CONTEXT_TOKENS`` or more
+tokens (``infer_state.max_decoding_len``), and ``decode`` otherwise (the
+Qwen3-0.6B Draft).
 """
 from __future__ import annotations
 
@@ -21,14 +26,15 @@ import torch
 from .. import _lib
 from .._workspace import attention_workspace
 
-_MODES = {"auto": None, "decode": _lib.NEB_ATTN_DECODE, "verify": _lib.NEB_ATTN_VERIFY}
+_MODES = {"auto": None, "decode": _lib.NEB_ATTN_DECODE, "verify": _lib.NEB_ATTN_VERIFY,
+          "verify_long": _lib.NEB_ATTN_VERIFY_LONG}
 _mode = os.environ.get("NEB_PAGED_ATTENTION", "auto").lower()
 if _mode not in _MODES:
     raise ValueError(f"NEB_PAGED_ATTENTION must be one of {sorted(_MODES)} (got {_mode!r})")
 
 
 def set_kernel(mode: str) -> None:
-    """Select ``"auto"``, ``"decode"`` or ``"verify"`` for later calls."""
+    """Select ``"auto"``, ``"decode"``, ``"verify"`` or ``"verify_long"`` for later calls."""
     global _mode
     if mode not in _MODES:
         raise ValueError(f"kernel must be one of {sorted(_MODES)}")
@@ -43,22 +49,39 @@ VERIFY_BUILT = os.environ.get("NEB_VERIFY_BUILT", "1") == "1"
 
 
 DECODE_RATIOS = (1, 2, 4, 8)  # q/kv head ratios the CUDA-core kernel is built for
+# Longest row (tokens) from which ``auto`` takes the long-context verify kernel:
+# below it the per-launch fixed costs dominate and ``verify`` is faster.
+LONG_CONTEXT_TOKENS = 8192
 
 
-def choose_kernel(num_q_heads: int, num_kv_heads: int, num_rows: int = 0) -> int:
-    """Tensor-core kernel for GQA ratios 4..16 (the rows x heads of a request
+def choose_kernel(num_q_heads: int, num_kv_heads: int, num_rows: int = 0, max_len: int | None = None) -> int:
+    """Tensor-core kernels for GQA ratios 4..16 (the rows x heads of a request
     fill its MMA tiles) and for every ratio the CUDA-core kernel is not built
-    for (3, 5, 6, 7, 9..16), up to its row limit; the CUDA-core kernel for
-    ratios 1 and 2 and for batches beyond that limit."""
+    for (3, 5, 6, 7, 9..16), up to their row limit (the long-context variant
+    when ``max_len``, the batch's longest row, reaches ``LONG_CONTEXT_TOKENS``);
+    the CUDA-core kernel for ratios 1 and 2 and for batches beyond that limit."""
     forced = _MODES[_mode]
     if forced is not None:
         return forced
     gqa = num_q_heads // num_kv_heads
-    fits_verify = VERIFY_BUILT and 1 <= gqa <= 16 and \
-        num_rows <= _lib.lib.neb_attention_max_rows(_lib.NEB_ATTN_VERIFY)
-    if fits_verify and (gqa >= 4 or gqa not in DECODE_RATIOS):
-        return _lib.NEB_ATTN_VERIFY
+    if VERIFY_BUILT and (gqa >= 4 or gqa not in DECODE_RATIOS):
+        if max_len is not None and max_len >= LONG_CONTEXT_TOKENS and 1 <= gqa <= 64 and \
+                num_rows <= _lib.lib.neb_attention_max_rows(_lib.NEB_ATTN_VERIFY_LONG):
+            return _lib.NEB_ATTN_VERIFY_LONG
+        if gqa <= 16 and num_rows <= _lib.lib.neb_attention_max_rows(_lib.NEB_ATTN_VERIFY):
+            return _lib.NEB_ATTN_VERIFY
     return _lib.NEB_ATTN_DECODE
+
+
+_ENTRY = {}
+
+
+def _entry(kernel: int):
+    if not _ENTRY:
+        _ENTRY.update({_lib.NEB_ATTN_DECODE: _lib.lib.neb_paged_attention_decode,
+                       _lib.NEB_ATTN_VERIFY: _lib.lib.neb_paged_attention_verify,
+                       _lib.NEB_ATTN_VERIFY_LONG: _lib.lib.neb_paged_attention_verify_long})
+    return _ENTRY[kernel]
 
 
 def _check_tensors(q, k_cache, v_cache, block_table, seq_lens, seq_ids, o):
@@ -80,20 +103,22 @@ def paged_attention_raw(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
                         block_table: torch.Tensor, seq_lens: torch.Tensor, seq_ids: torch.Tensor,
                         cur_layer: int, softmax_scale: float, o: torch.Tensor,
                         kernel: int | None = None, workspace: torch.Tensor | None = None,
-                        stream: torch.cuda.Stream | None = None) -> None:
-    """Tensor-level entry: ``o[r] = attention(q[r], KV of seq_ids[r] up to seq_lens[r])``."""
+                        stream: torch.cuda.Stream | None = None, max_len: int | None = None) -> None:
+    """Tensor-level entry: ``o[r] = attention(q[r], KV of seq_ids[r] up to seq_lens[r])``.
+
+    ``max_len`` (optional, the longest of ``seq_lens``, known on the host) lets
+    ``auto`` pick the long-context kernel."""
     _check_tensors(q, k_cache, v_cache, block_table, seq_lens, seq_ids, o)
     num_rows, num_q_heads, head_dim = q.shape
     num_blocks, num_layers, num_kv_heads, block_size, _ = k_cache.shape
     if o.shape != q.shape or seq_lens.shape[0] != num_rows or seq_ids.shape[0] != num_rows:
         raise ValueError("q, o, seq_lens and seq_ids disagree on the number of rows")
     if kernel is None:
-        kernel = choose_kernel(num_q_heads, num_kv_heads, num_rows)
+        kernel = choose_kernel(num_q_heads, num_kv_heads, num_rows, max_len)
     stream = stream or torch.cuda.current_stream(q.device)
     if workspace is None:
         workspace = attention_workspace(kernel, q.device, stream, num_rows, num_q_heads, num_kv_heads)
-    fn = _lib.lib.neb_paged_attention_verify if kernel == _lib.NEB_ATTN_VERIFY else _lib.lib.neb_paged_attention_decode
-    rc = fn(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
+    rc = _entry(kernel)(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
             block_table.shape[0], block_table.shape[1], seq_lens.data_ptr(), seq_ids.data_ptr(),
             num_rows, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks, num_layers,
             cur_layer, float(softmax_scale), o.data_ptr(), workspace.data_ptr(), workspace.numel(),
@@ -119,4 +144,4 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     q3 = q.view(infer_state.num_decoding_seqs, model_config.num_q_heads, model_config.head_dim)
     paged_attention_raw(q3, k_cache, v_cache, block_table, infer_state.decoding_seq_lens,
                         infer_state.seq_ids[infer_state.num_prefill_seqs:], cur_layer,
-                        infer_state.softmax_scale, o3)
+                        infer_state.softmax_scale, o3, max_len=getattr(infer_state, "max_decoding_len", None))

@@ -17,12 +17,13 @@ GOLD_ATOL = 4e-3
 
 from nebulasd_b200.kernels.paged_attn import VERIFY_BUILT  # noqa: E402
 
-KERNELS = ["decode", "verify"] if VERIFY_BUILT else ["decode"]
+KERNELS = ["decode", "verify", "verify_long"] if VERIFY_BUILT else ["decode"]
 
 
 def _kernel_id(name):
     from nebulasd_b200 import _lib
-    return {"decode": _lib.NEB_ATTN_DECODE, "verify": _lib.NEB_ATTN_VERIFY}[name]
+    return {"decode": _lib.NEB_ATTN_DECODE, "verify": _lib.NEB_ATTN_VERIFY,
+            "verify_long": _lib.NEB_ATTN_VERIFY_LONG}[name]
 
 
 def run_attention(c, kernel, dev, workspace=None):
@@ -107,10 +108,28 @@ GQA_SHAPES["gqa5_ragged"] = dict(num_requests=6, depth=[8, 0, 3, 11, 1, 5], ctx_
 
 
 @pytest.mark.skipif(not VERIFY_BUILT, reason="verify kernel not built")
+@pytest.mark.parametrize("kernel", ["verify", "verify_long"])
 @pytest.mark.parametrize("shape", sorted(GQA_SHAPES))
-def test_verify_every_gqa_ratio_matches_oracle(shape, cuda):
+def test_verify_every_gqa_ratio_matches_oracle(kernel, shape, cuda):
     c = batch_case(3000 + sorted(GQA_SHAPES).index(shape), **GQA_SHAPES[shape])
-    torch.testing.assert_close(run_attention(c, "verify", cuda), oracle_of(c), atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(run_attention(c, kernel, cuda), oracle_of(c), atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.skipif(not VERIFY_BUILT, reason="verify kernel not built")
+@pytest.mark.parametrize("kernel", ["verify", "verify_long"])
+def test_long_prefix_batch_matches_oracle(kernel, cuda):
+    """Prefixes of 8 K - 20 K tokens (many 128-token stages per unit, units split across CTAs)."""
+    c = batch_case(5150, num_requests=3, depth=[4, 8, 0], ctx_lo=8192, ctx_hi=20000, num_q_heads=32,
+                   num_kv_heads=8, pool_blocks=4000)
+    torch.testing.assert_close(run_attention(c, kernel, cuda), oracle_of(c), atol=ATOL, rtol=RTOL)
+
+
+def test_auto_picks_long_kernel_from_max_len():
+    from nebulasd_b200 import _lib
+    from nebulasd_b200.kernels.paged_attn import LONG_CONTEXT_TOKENS, choose_kernel
+    assert choose_kernel(32, 8, 80, 4100) == _lib.NEB_ATTN_VERIFY
+    assert choose_kernel(32, 8, 80, LONG_CONTEXT_TOKENS) == _lib.NEB_ATTN_VERIFY_LONG
+    assert choose_kernel(16, 8, 64, 40000) == _lib.NEB_ATTN_DECODE
 
 
 def test_auto_dispatch_serves_every_ratio_up_to_16(cuda):
