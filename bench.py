@@ -70,6 +70,8 @@ def _args():
     ap.add_argument("--layers", type=int, default=None,
                     help="override the workload's layer count (profiling: a small pool, same per-call shape)")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s clock-sampling soak (profiling runs)")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the secondary figures (reference kernels on this GPU, configs 2, 2b and 4)")
     return ap.parse_args()
 
 
@@ -236,47 +238,25 @@ def run_ours(args):
     achieved_gbs = per_step / layers / (launch_ms * 1e-3) / 1e9
     peak, peak_kind = _peaks()
 
-    # ---- e2e through the drop-in API with host buffers
+    # ---- e2e through the drop-in API with host buffers, copies overlapped
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 50))
-    R, H, D = b.q.shape
-    q_host = torch.empty((layers, R, H, D), dtype=torch.float16, pin_memory=True)
-    q_host.copy_(b.q.cpu().unsqueeze(0).expand(layers, R, H, D))
-    o_host = torch.empty_like(q_host, pin_memory=True)
-    lens_host = b.seq_lens.cpu().pin_memory()
-    ids_host = b.seq_ids.cpu().pin_memory()
-    bt_host = b.block_table.cpu().pin_memory()
-    q_dev = torch.empty((layers, R, H, D), dtype=torch.float16, device=dev)
-    o_dev = torch.empty((layers, R, H * D), dtype=torch.float16, device=dev)
-    lens_dev, ids_dev, bt_dev = torch.empty_like(b.seq_lens), torch.empty_like(b.seq_ids), torch.empty_like(b.block_table)
-    from nebulasd_b200.workloads import decode_infer_state
-    st = decode_infer_state(lens_dev, ids_dev, b.seq_lens_list, b.num_kv_heads, scale)
-    mc = types.SimpleNamespace(num_q_heads=H, num_kv_heads=b.num_kv_heads, head_dim=D, num_layers=layers)
-    ec = types.SimpleNamespace(block_size=16, max_blocks_per_seq=b.block_table.shape[1])
+    e2e_value, h2d, d2h = measure_e2e(b, layers, dev, world, e2e_steps, scale, barrier)
 
-    def e2e_step():
-        q_dev.copy_(q_host, non_blocking=True)
-        lens_dev.copy_(lens_host, non_blocking=True)
-        ids_dev.copy_(ids_host, non_blocking=True)
-        bt_dev.copy_(bt_host, non_blocking=True)
-        for layer in range(layers):
-            paged_attention(q_dev[layer], b.k_cache, b.v_cache, bt_dev, mc, ec, st, layer, o_dev[layer])
-        o_host.view(layers, R, H * D).copy_(o_dev, non_blocking=True)
+    # ---- requests/s, and strong scaling (16 requests in total over the ranks)
+    requests_per_s = world * cfg["num_requests"] * args.steps / (ms_max * 1e-3)
+    strong = measure_strong(b, layers, cfg, dev, world, rank, kernel, scale, barrier, ms_max / args.steps)
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    f1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    ems = max_over_ranks(f0.elapsed_time(f1), dev, world)
-    e2e_value = per_step * e2e_steps * world / (ems * 1e-3) / 1e12
-    h2d = q_host.numel() * 2 + lens_host.numel() * 4 + ids_host.numel() * 4 + bt_host.numel() * 4
-    d2h = o_host.numel() * 2
+    # ---- secondary figures on one GPU: the reference's own kernels on this
+    # B200, the other configs' kernels (single-GPU runs only)
+    secondary = {}
+    if world == 1 and not args.no_secondary:
+        secondary["reference_gpu"] = _guard(lambda: reference_gpu_bar(b, layers, scale, launch_ms))
+        k_cache_free(b)  # the headline pool, before the other configs' pools
+        torch.cuda.empty_cache()
+        secondary["draft_decode_0p6b"] = _guard(lambda: secondary_attention("draft_decode_0p6b", dev, 5))
+        secondary["fused_qk_norm_rope_store_0p6b"] = _guard(lambda: fused_bar(dev))
+        secondary["long_verify_8b_k4"] = _guard(lambda: secondary_attention("long_verify_8b_k4", dev, 3))
+        secondary["long_verify_8b_k8"] = _guard(lambda: secondary_attention("long_verify_8b_k8", dev, 3))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -301,12 +281,279 @@ def run_ours(args):
                      "traffic": _traffic(args.workload, kname),
                      "bytes_per_launch": per_step // layers, "launch_us": round(launch_ms * 1e3, 3)},
         "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": e2e_steps, "api": "nebulasd_b200.kernels.paged_attention"},
+                "steps": e2e_steps, "api": "nebulasd_b200.kernels.paged_attention",
+                "copies": "per-layer q rows H2D and o rows D2H on two side streams, overlapped with attention"},
+        "requests_per_s": round(requests_per_s, 1),
+        "strong_scaling": strong,
         "gpu_launches": args.steps * layers,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
+    line.update(secondary)
     print(json.dumps(line), flush=True)
+
+
+def _guard(fn):
+    """A secondary measurement, or why it is unavailable (it never costs the headline line)."""
+    try:
+        return fn()
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
+def k_cache_free(b):
+    b.k_cache = b.v_cache = None
+
+
+def measure_e2e(b, layers, dev, world, steps, scale, barrier):
+    """Same metric through ``nebulasd_b200.kernels.paged_attention`` with HOST buffers.
+
+    Every step copies its inputs from pinned host memory (the block table,
+    lengths and seq ids, then each layer's q rows) on an H2D stream and each
+    layer's o rows back on a D2H stream; attention of layer l waits only for
+    its own q rows, and the copy-out of layer l runs while layer l + 1 computes
+    (the pipelined host interface a serving loop would use).  The timed region
+    covers every copy.
+    """
+    from nebulasd_b200.kernels import paged_attention
+    from nebulasd_b200.workloads import decode_infer_state
+    R, H, D = b.q.shape
+    q_host = torch.empty((layers, R, H, D), dtype=torch.float16, pin_memory=True)
+    q_host.copy_(b.q.cpu().unsqueeze(0).expand(layers, R, H, D))
+    o_host = torch.empty((layers, R, H * D), dtype=torch.float16, pin_memory=True)
+    lens_host = b.seq_lens.cpu().pin_memory()
+    ids_host = b.seq_ids.cpu().pin_memory()
+    bt_host = b.block_table.cpu().pin_memory()
+    q_dev = torch.empty((layers, R, H, D), dtype=torch.float16, device=dev)
+    o_dev = torch.empty((layers, R, H * D), dtype=torch.float16, device=dev)
+    lens_dev, ids_dev, bt_dev = torch.empty_like(b.seq_lens), torch.empty_like(b.seq_ids), torch.empty_like(b.block_table)
+    st = decode_infer_state(lens_dev, ids_dev, b.seq_lens_list, b.num_kv_heads, scale)
+    mc = types.SimpleNamespace(num_q_heads=H, num_kv_heads=b.num_kv_heads, head_dim=D, num_layers=layers)
+    ec = types.SimpleNamespace(block_size=16, max_blocks_per_seq=b.block_table.shape[1])
+    comp = torch.cuda.current_stream(dev)
+    h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    tables_ready, tables_used = ev(), ev()
+    q_ready, q_used = [ev() for _ in range(layers)], [ev() for _ in range(layers)]
+    o_ready, o_drained = [ev() for _ in range(layers)], [ev() for _ in range(layers)]
+
+    def e2e_step():
+        with torch.cuda.stream(h2d_s):
+            h2d_s.wait_event(tables_used)  # the previous step's last layer is done with them
+            lens_dev.copy_(lens_host, non_blocking=True)
+            ids_dev.copy_(ids_host, non_blocking=True)
+            bt_dev.copy_(bt_host, non_blocking=True)
+            tables_ready.record(h2d_s)
+            for layer in range(layers):
+                h2d_s.wait_event(q_used[layer])
+                q_dev[layer].copy_(q_host[layer], non_blocking=True)
+                q_ready[layer].record(h2d_s)
+        comp.wait_event(tables_ready)
+        for layer in range(layers):
+            comp.wait_event(q_ready[layer])
+            comp.wait_event(o_drained[layer])
+            paged_attention(q_dev[layer], b.k_cache, b.v_cache, bt_dev, mc, ec, st, layer, o_dev[layer])
+            q_used[layer].record(comp)
+            o_ready[layer].record(comp)
+            with torch.cuda.stream(d2h_s):
+                d2h_s.wait_event(o_ready[layer])
+                o_host[layer].copy_(o_dev[layer], non_blocking=True)
+                o_drained[layer].record(d2h_s)
+        tables_used.record(comp)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(comp)
+    h2d_s.wait_event(f0)
+    for _ in range(steps):
+        e2e_step()
+    comp.wait_event(o_drained[-1])
+    f1.record(comp)
+    torch.cuda.synchronize()
+    barrier()
+    ems = max_over_ranks(f0.elapsed_time(f1), dev, world)
+    value = step_bytes(b, layers) * steps * world / (ems * 1e-3) / 1e12
+    h2d = q_host.numel() * 2 + lens_host.numel() * 4 + ids_host.numel() * 4 + bt_host.numel() * 4
+    d2h = o_host.numel() * 2
+    return value, h2d, d2h
+
+
+def measure_strong(b, layers, cfg, dev, world, rank, kernel, scale, barrier, headline_ms_per_step):
+    """Strong scaling: the headline's 16 requests in total, split evenly over the ranks."""
+    total = cfg["num_requests"]
+    if world == 1:
+        return {"requests_total": total, "requests_per_gpu": total, "ms_per_step": round(headline_ms_per_step, 4),
+                "requests_per_s": round(total / (headline_ms_per_step * 1e-3), 1)}
+    from nebulasd_b200.kernels import paged_attention_raw
+    from nebulasd_b200.workloads import make_paged_batch
+    per = max(1, total // world)
+    sub = dict(cfg)
+    sub["num_requests"] = per
+    sb = make_paged_batch(4321 + 7919 * rank, num_layers=layers, cur_layer=0, device=dev,
+                          cache=(b.k_cache, b.v_cache), **sub)
+    o = torch.empty_like(sb.q)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for layer in range(layers):
+            paged_attention_raw(sb.q, sb.k_cache, sb.v_cache, sb.block_table, sb.seq_lens, sb.seq_ids, layer, scale,
+                                o, kernel=kernel, stream=stream)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    steps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1), dev, world) / steps
+    return {"requests_total": per * world, "requests_per_gpu": per, "ms_per_step": round(ms, 4),
+            "requests_per_s": round(per * world / (ms * 1e-3), 1)}
+
+
+def _time_steps(fn, steps, warmup=2):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def reference_gpu_bar(b, layers, scale, our_launch_ms):
+    """The reference's own Triton ``paged_attention`` (phase 1 + phase 2,
+    ``swiftLLM/swiftllm/worker/kernels/paged_attn.py:152-222``), JIT-compiled by
+    Triton for this GPU, on the headline batch and pool (one call per layer, its
+    own split-K choice ``worker/model.py:380-384``), timed with CUDA events."""
+    from baseline import reference as R
+    if not R.available():
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    pa = R.swiftllm("worker.kernels.paged_attn")
+    from nebulasd_b200.workloads import decode_infer_state
+    R_, H, D = b.q.shape
+    st = decode_infer_state(b.seq_lens, b.seq_ids, b.seq_lens_list, b.num_kv_heads, scale)
+    mc = types.SimpleNamespace(num_q_heads=H, num_kv_heads=b.num_kv_heads, head_dim=D, num_layers=layers)
+    ec = types.SimpleNamespace(block_size=16, max_blocks_per_seq=b.block_table.shape[1])
+    o = torch.empty((R_, H * D), dtype=torch.float16, device=b.q.device)
+
+    def step():
+        for layer in range(layers):
+            pa.paged_attention(b.q, b.k_cache, b.v_cache, b.block_table, mc, ec, st, layer, o)
+
+    t0 = time.perf_counter()
+    step()  # JIT compile on first use
+    torch.cuda.synchronize()
+    compile_s = time.perf_counter() - t0
+    ms = _time_steps(step, 3, warmup=1)
+    per_launch = ms / layers
+    bytes_per_launch = step_bytes(b, 1)
+    return {"impl": "reference Triton paged_attention (phase 1 + phase 2), same batch and pool",
+            "value": round(bytes_per_launch / (per_launch * 1e-3) / 1e12, 4), "unit": UNIT,
+            "launch_us": round(per_launch * 1e3, 2), "ours_speedup": round(per_launch / our_launch_ms, 2),
+            "seq_block_size": st.seq_block_size, "first_call_s": round(compile_s, 1)}
+
+
+def secondary_attention(workload, dev, steps):
+    """Another config's attention through the same drop-in op (auto kernel choice)."""
+    from nebulasd_b200 import _lib
+    from nebulasd_b200.kernels import paged_attention_raw
+    from nebulasd_b200.kernels.paged_attn import choose_kernel
+    b, layers, cfg = build_workload(workload, 1234, dev)
+    kernel = choose_kernel(b.num_q_heads, b.num_kv_heads, int(b.q.shape[0]), max(b.seq_lens_list))
+    o = torch.empty_like(b.q)
+    scale = b.q.shape[-1] ** -0.5
+    reps = max(1, 36 // layers)
+
+    def step():
+        for _ in range(reps):
+            for layer in range(layers):
+                paged_attention_raw(b.q, b.k_cache, b.v_cache, b.block_table, b.seq_lens, b.seq_ids, layer, scale,
+                                    o, kernel=kernel)
+
+    ms = _time_steps(step, steps)
+    launch_ms = ms / (reps * layers)
+    per_launch = step_bytes(b, 1)
+    peak, _ = _peaks()
+    tbps = per_launch / (launch_ms * 1e-3) / 1e12
+    out = {"value": round(tbps, 4), "unit": UNIT, "frac_of_measured_peak": round(tbps * 1e3 / peak, 4),
+           "launch_us": round(launch_ms * 1e3, 2), "bytes_per_launch": per_launch,
+           "kernel": {_lib.NEB_ATTN_DECODE: "decode", _lib.NEB_ATTN_VERIFY: "verify",
+                      _lib.NEB_ATTN_VERIFY_LONG: "verify_long"}[kernel],
+           "requests": cfg["num_requests"], "depth": cfg["depth"], "ctx": [cfg["ctx_lo"], cfg["ctx_hi"]],
+           "num_layers": layers}
+    k_cache_free(b)
+    torch.cuda.empty_cache()
+    return out
+
+
+def fused_bar(dev):
+    """Config 2b: QK-RMSNorm + RoPE + KV store of the Draft's 64 decode tokens
+    (Qwen3-0.6B: 16 q / 8 kv heads, 28-layer pool), our single launch against
+    the reference's four Triton launches (``transformer_layer.py:114-143``) on
+    the same inputs."""
+    from nebulasd_b200.kernels import qk_norm_rope_store
+    from nebulasd_b200.workloads import CONFIGS, decode_infer_state, make_paged_batch
+    from baseline import reference as R
+    cfg = dict(CONFIGS["draft_decode_0p6b"])
+    layers = cfg.pop("num_layers")
+    cfg["pool_blocks"] = 8192  # holds the batch's blocks; smaller than config 2's pool, so the set-up is short
+    b = make_paged_batch(77, num_layers=layers, cur_layer=0, device=dev, **cfg)
+    T, H, D = b.q.shape
+    hk = b.num_kv_heads
+    g = torch.Generator(device=dev).manual_seed(78)
+    k = torch.randn((T, hk, D), generator=g, device=dev, dtype=torch.float16)
+    v = torch.randn((T, hk, D), generator=g, device=dev, dtype=torch.float16)
+    wq = (1 + 0.02 * torch.randn(D, generator=g, device=dev)).half()
+    wk = (1 + 0.02 * torch.randn(D, generator=g, device=dev)).half()
+    pos = (b.seq_lens - 1).long()
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+    freqs = torch.outer(pos.float(), inv)
+    st = decode_infer_state(b.seq_lens, b.seq_ids, b.seq_lens_list, hk, D ** -0.5)
+    st.position_cos, st.position_sin = torch.cos(freqs).half(), torch.sin(freqs).half()
+    st.num_prefill_seqs, st.num_prefill_tokens = 0, 0
+    mc = types.SimpleNamespace(num_q_heads=H, num_kv_heads=hk, head_dim=D, num_layers=layers, rms_norm_eps=1e-6)
+    ec = types.SimpleNamespace(block_size=16, max_blocks_per_seq=b.block_table.shape[1])
+    q0 = b.q.clone()
+    k0 = k.clone()
+    layer = layers // 2
+
+    def ours():
+        qk_norm_rope_store(q0, k0, v, wq, wk, 1e-6, b.k_cache, b.v_cache, b.block_table, mc, ec, st, layer)
+
+    out = {"tokens": T, "ours_launches": 1, "ours_us": round(_time_steps(ours, 200, 5) * 1e3, 2)}
+    # moved bytes: q and k read and written, v read, k and v written to the cache
+    out["bytes"] = (2 * q0.numel() + 2 * k0.numel() + v.numel() + 2 * k0.numel()) * 2
+    if R.available():
+        rm = R.swiftllm("worker.kernels.rmsnorm")
+        ro = R.swiftllm("worker.kernels.rotary_emb")
+        kv = R.swiftllm("worker.kernels.kvcache_mgmt")
+
+        def ref():
+            rm.rmsnorm_inplace(q0.view(-1, D), wq, 1e-6)
+            rm.rmsnorm_inplace(k0.view(-1, D), wk, 1e-6)
+            ro.rotary_embedding_inplace(q0, k0, st)
+            kv.store_kvcache(k0, v, b.k_cache, b.v_cache, b.block_table, mc, ec, st, layer)
+
+        ref()  # JIT compile on first use
+        torch.cuda.synchronize()
+        out["reference_launches"] = 4
+        out["reference_us"] = round(_time_steps(ref, 200, 5) * 1e3, 2)
+        out["ours_speedup"] = round(out["reference_us"] / out["ours_us"], 3)
+    k_cache_free(b)
+    torch.cuda.empty_cache()
+    return out
 
 
 def cpu_baseline(workload: str, budget_s: float):
@@ -371,13 +618,22 @@ def run_reference(args):
 
 
 def run_hostkv(args):
-    """HostKV restore/writeback bandwidth (rank 0 only; the copies are per GPU and PCIe-bound)."""
+    """HostKV restore/writeback bandwidth (rank 0 only; the copies are per GPU and PCIe-bound).
+
+    The arena, extents and plans are the reference's own (``SharedHostKVArena``,
+    ``CopyRegion``, ``CopyPlan`` from ``baseline/_ref``); without them the line
+    says unavailable."""
     world, rank, local = _dist()
     if rank != 0:
         return
     import numpy as np
+    from baseline import reference as R
     from nebulasd_b200.hostkv import NativeCopyBackend
-    from tests.hostkv_support import Arena, CopyPlan, CopyRegion
+    metric = "HostKV restore GB/s (both planes, Qwen3-8B blocks)"
+    if not R.available():
+        print(json.dumps({"metric": metric, "unavailable": "reference not installed under baseline/_ref"}), flush=True)
+        return
+    arena_mod, tr = R.nebulasd("kv.arena"), R.nebulasd("kv.transfer")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     layers, hk = 36, 8
@@ -386,15 +642,22 @@ def run_hostkv(args):
     k_cache = torch.zeros(shape, dtype=torch.float16, device=dev)
     v_cache = torch.zeros(shape, dtype=torch.float16, device=dev)
     block_bytes = k_cache[0].numel() * 2
-    arena = Arena(host_blocks, block_bytes, "torch.float16", shape[1:])
+    try:
+        arena = arena_mod.SharedHostKVArena.create(total_blocks=host_blocks, block_bytes=block_bytes,
+                                                   dtype=str(k_cache.dtype), kv_block_shape=shape[1:])
+    except OSError as e:  # POSIX shared memory smaller than the 2.4 GB arena
+        print(json.dumps({"metric": metric, "unavailable": f"shared-memory arena: {e}"}), flush=True)
+        return
     rng = np.random.default_rng(1234)
-    arena.buf.fill(7)  # the bytes do not matter to a bit copy over PCIe
     # Four requests' block runs (ctx U[1 K, 4 K] tokens): host extents and GPU
     # ranges disjoint; at most 4 * 256 blocks, so GPU blocks 200.. stay below 1280.
     counts = rng.integers(64, 257, 4).tolist()
     host_off = np.cumsum([0] + counts[:-1]).tolist()
     gpu_off = (np.cumsum([0] + counts[:-1]) + 200).tolist()
-    regions = tuple(CopyRegion(arena.make_extent(h, c), g, 0, c) for h, c, g in zip(host_off, counts, gpu_off))
+    extents = [arena.make_extent(request_slot=i, request_epoch=1, host_slot=i, host_slot_generation=1,
+                                 writer_lease_generation=1, offset_blocks=h, capacity_blocks=c)
+               for i, (h, c) in enumerate(zip(host_off, counts))]
+    regions = tuple(tr.CopyRegion(e, g, 0, c) for e, g, c in zip(extents, gpu_off, counts))
     moved = 2 * sum(counts) * block_bytes  # both planes
     out = {}
     for mode in ("auto", "kernel", "memcpy"):
@@ -402,7 +665,7 @@ def run_hostkv(args):
         be.initialize()
         res = {}
         for direction in ("H2D", "D2H"):
-            plan = CopyPlan(direction, regions)
+            plan = tr.CopyPlan(direction, regions)
             for _ in range(max(args.warmup, 3)):
                 be.launch(plan).synchronize()
             ms = [0.0]
@@ -436,7 +699,7 @@ def run_hostkv(args):
         "n_gpus": 1, "steps": max(1, min(args.steps, 20)), "warmup": max(args.warmup, 3),
         "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
         "config": {"workload": "hostkv_copy", "requests": 4, "blocks": counts, "block_bytes": block_bytes,
-                   "bytes_per_plan": moved},
+                   "bytes_per_plan": moved, "arena": "reference SharedHostKVArena (POSIX shared memory)"},
         "writeback_gbs": round(out["auto"]["D2H"], 2),
         "kernel_mode": {k: round(v, 2) for k, v in out["kernel"].items()},
         "memcpy_mode": {k: round(v, 2) for k, v in out["memcpy"].items()},
@@ -445,6 +708,8 @@ def run_hostkv(args):
                      "peak_d2h": round(peak["D2H"], 2)},
         "e2e": {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": moved, "d2h_bytes_per_step": 0},
     }
+    arena.close()
+    arena.unlink()
     print(json.dumps(line), flush=True)
 
 

@@ -88,26 +88,9 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
   return v;
 }
 
-// Atomic add at GPU scope with acquire-release semantics: the writes that
-// precede it (in causality order) are visible to whoever observes its result.
-__device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
-  return old;
-}
-
 // ---------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
-}
-
-// 2D tiled load of one box into shared memory, completing on `bar` (no multicast).
-__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
 }
 
 // L2 policy for data read once (evicted before other lines).
@@ -117,7 +100,8 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return pol;
 }
 
-// As tma_load_2d, with an L2 cache policy for the box.
+// 2D tiled load of one box into shared memory with an L2 cache policy,
+// completing on `bar` (no multicast).
 __device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* tmap, uint64_t* bar, int x, int y,
                                                  uint64_t policy) {
   asm volatile(
@@ -134,12 +118,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
-}
-
-// Prefetch one box of a 2D tensor map into L2 (no shared memory, no barrier).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)
-               : "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05
@@ -267,18 +245,6 @@ __device__ __forceinline__ void tmem_ld_32x32b_cols(uint32_t taddr, uint32_t* r)
 // be scheduled before this one ends.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
-
-// Per-warpgroup register split: every warp of a warpgroup executes the same
-// setmaxnreg; .dec returns registers to the CTA's pool (the registers it was
-// launched with), .inc takes them from it, waiting until they are free.
-template <uint32_t kRegs>
-__device__ __forceinline__ void setmaxnreg_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
-}
-template <uint32_t kRegs>
-__device__ __forceinline__ void setmaxnreg_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
-}
 
 // 16-byte shared-memory store.
 __device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
