@@ -34,7 +34,10 @@ def attention_workspace(kernel: int, device: torch.device, stream: torch.cuda.St
         if buf is None or buf.numel() < need:
             # Round up so that slowly growing batches do not reallocate every call.
             size = max(need, 2 * buf.numel() if buf is not None else 0, 1 << 20)
-            with torch.cuda.stream(stream):
+            # Long-lived buffers are never inference tensors, even when the first
+            # call comes from inside ``torch.inference_mode()`` (the reference's
+            # model forward): callers may update them in place outside it.
+            with torch.cuda.stream(stream), torch.inference_mode(False):
                 buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", index))
             _buffers[key] = buf
         return buf
@@ -63,6 +66,7 @@ def error_word(device: torch.device) -> torch.Tensor:
     with _lock:
         t = _error_words.get(index)
         if t is None:
-            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+            with torch.inference_mode(False):  # see attention_workspace
+                t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
             _error_words[index] = t
         return t

@@ -136,3 +136,20 @@ def test_store_bad_block_recorded(cuda):
     torch.cuda.synchronize()
     assert int(err.item()) & 1
     err.zero_()
+
+
+def test_buffers_first_made_under_inference_mode_are_normal_tensors(cuda):
+    """The reference runs its forward under ``torch.inference_mode()``; the
+    per-device error word and attention workspace made on a first call there
+    must still accept in-place updates outside it."""
+    from nebulasd_b200 import _lib, _workspace
+    _workspace.release_all()
+    _workspace._error_words.clear()
+    stream = torch.cuda.current_stream(cuda)
+    with torch.inference_mode():
+        err = _workspace.error_word(cuda)
+        ws = _workspace.attention_workspace(_lib.NEB_ATTN_VERIFY, cuda, stream, 8, 32, 8)
+    assert not err.is_inference() and not ws.is_inference()
+    err.zero_()
+    ws[:1].zero_()
+    torch.cuda.synchronize()
