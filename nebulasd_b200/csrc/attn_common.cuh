@@ -124,27 +124,29 @@ __device__ inline void merge_unit_warp(const AttnParams& p, int first_row, int n
 }
 
 // The same merge spread over `nthreads` threads (tid in [0, nthreads)): a
-// thread owns (unit row, 4-column chunk) pairs, four at a time, and issues the
+// thread owns (unit row, 4-column chunk) pairs, kQ at a time, and issues the
 // loads of all their slots (up to four slots per round) before using any, so
-// that a merge costs one or two memory round trips.  Slots fold in order with
-// a running maximum.
+// that a merge costs one memory round trip when nthreads * kQ covers the
+// unit.  Slots fold in order with a running maximum; the result does not
+// depend on kQ or nthreads.
+template <int kQ>
 static __device__ __noinline__ void merge_unit_threads(const AttnParams& p, int first_row, int nrows, int kv_head,
                                                        int gqa, long long w0, long long w1, int tid, int nthreads) {
   const int npairs = nrows * gqa * 32;
-  for (int base = tid; base < npairs; base += 4 * nthreads) {
-    float mx[4], den[4];
-    float4 acc[4];
+  for (int base = tid; base < npairs; base += kQ * nthreads) {
+    float mx[kQ], den[kQ];
+    float4 acc[kQ];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < kQ; ++q) {
       mx[q] = neg_inf();
       den[q] = 0.f;
       acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     for (long long wb = w0; wb <= w1; wb += 4) {
-      float le[4][4];
-      float4 v[4][4];
+      float le[kQ][4];
+      float4 v[kQ][4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < kQ; ++q) {
         const int idx = base + q * nthreads;
         const int j = idx >> 5, c = idx & 31;
 #pragma unroll
@@ -159,7 +161,7 @@ static __device__ __noinline__ void merge_unit_threads(const AttnParams& p, int 
         }
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < kQ; ++q) {
         const float cm = fmaxf(fmaxf(le[q][0], le[q][1]), fmaxf(le[q][2], le[q][3]));
         if (cm == neg_inf()) continue;
         if (cm > mx[q]) {
@@ -179,7 +181,7 @@ static __device__ __noinline__ void merge_unit_threads(const AttnParams& p, int 
       }
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < kQ; ++q) {
       const int idx = base + q * nthreads;
       if (idx >= npairs) continue;
       const int j = idx >> 5, c = idx & 31;

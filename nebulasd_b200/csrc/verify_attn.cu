@@ -34,7 +34,7 @@
 //   warp 7      P V issuer (one thread): O += P V (V an MN-major operand) into
 //               a TMEM accumulator (M=64, N=128).
 // A unit split across CTAs is merged by the CTA that finishes it last (see
-// piece_epilogue and finish_first_unit).
+// piece_epilogue and finish_units).
 //
 // Each role is an out-of-line function and the two producers share one, so
 // that the instruction cache holds every warp's hot loop at once: with more
@@ -63,11 +63,13 @@
 namespace neb {
 using namespace sm100;
 
-constexpr int kVThreads = 256;  // 8 warps: 0 K, 1 S, 2-5 softmax, 6 V, 7 P V
+constexpr int kVThreads = 384;  // 12 warps: 0 K, 1 S, 2-5 softmax, 6 V, 7 P V, 8-11 epilogue
 constexpr int kKWarp = 0;
 constexpr int kSWarp = 1;
 constexpr int kSoftmaxWarp0 = 2;
 constexpr int kSoftmaxThreads = 128;
+constexpr int kEpiWarp0 = 8;                              // epilogue warps: TMEM lane quadrants 0..3
+constexpr int kEpiThreads = 128;
 constexpr int kVWarp = 6;
 constexpr int kPVWarp = 7;
 constexpr int kStageBlocks = 4;                           // 16-token KV blocks per stage
@@ -82,11 +84,12 @@ constexpr int kMaxQRows = 64;                             // query rows per unit
 constexpr int kMaxGqa = 16;                               // a row's heads fit one 16-row chunk
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSBuf = 64;                            // S tile b at columns 64*b
-constexpr uint32_t kOCol = 256;                           // O: 128 columns
+constexpr uint32_t kOCol = 256;                           // O of piece i: 128 columns at kOCol + 128 * (i % 2)
 constexpr long long kWaitLimit = 4000000000LL;
 constexpr int kMaxDirectOthers = 3;                      // direct merge: at most 3 other pieces
 constexpr int kPieceCost = 8;                             // a piece's fixed cost, in tiles (plan.cuh CostSplit)
-static_assert(kStageCols <= (int)kSBuf && kStageR % 2 == 0 && kSBufs * kSBuf <= kOCol, "S tiles fit TMEM");
+static_assert(kStageCols <= (int)kSBuf && kStageR % 2 == 0 && kSBufs * kSBuf <= kOCol && kOCol + 256 <= kTmemCols,
+              "S tiles and both O buffers fit TMEM");
 static_assert(kSlotStages == 2 && (kStageBlocks & (kStageBlocks - 1)) == 0 && 2 * kSlotStages * kStageBlocks <= 32,
               "the producers fill a slot with two stages, one 64-column box per lane");
 
@@ -102,7 +105,8 @@ constexpr uint32_t kVOff = kKOff + kKRing * kSlotBytes;
 constexpr uint32_t kPAtom = kMaxQRows * 128;       // 64 rows x 64 fp16 of P (one swizzle column)
 constexpr uint32_t kPBuf = ((kStageCols + 63) / 64) * kPAtom;
 constexpr uint32_t kPOff = kVOff + kVRing * kSlotBytes;
-constexpr uint32_t kBarOff = kPOff + 2 * kPBuf;
+constexpr uint32_t kStatOff = kPOff + 2 * kPBuf;   // row max and sum of a piece: [2][64] float2
+constexpr uint32_t kBarOff = kStatOff + 2 * kMaxQRows * 8;
 constexpr uint32_t kPlanOff = kBarOff + 1024;
 static_assert(kHalf % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 
@@ -138,7 +142,10 @@ struct VerifyShared {
   uint64_t pv_done[2];
   uint64_t q_full[2];
   uint64_t q_empty[2];
-  uint64_t o_empty;
+  uint64_t o_full[2];            // P V of piece i's last stage done: O buffer i % 2 complete
+  uint64_t o_empty[2];           // the epilogue read O buffer i % 2 (one arrival per epilogue warp)
+  uint64_t st_full[2];           // the softmax wrote piece i's row statistics (one arrival per warp)
+  uint64_t st_empty[2];          // the epilogue read them
   uint64_t part_ready;           // softmax wrote the partial of the CTA's first piece (split, not last)
   uint64_t s_final;
   uint64_t pv_final;
@@ -146,6 +153,9 @@ struct VerifyShared {
   int32_t abort_flag;
   int32_t merge_mode;            // epilogue of the last piece: merge directly with the other partial
   int32_t first_last;            // the first piece's count completed its unit: merge it at the end
+  int32_t last_merge;            // the last piece's count completed its unit: merge it at the end
+  int32_t lm_g, lm_h;            // that unit's group and kv head
+  long long lm_w0, lm_w1;        // and its first and last workers
   int32_t blk[kFlagSlots][kStageBlocks];
 };
 static_assert(sizeof(VerifyShared) <= 1024, "barrier block fits its slot");
@@ -407,7 +417,6 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
   const int lane = threadIdx.x & 31;
-  if (lane == 0) tma_prefetch_desc(tmap);
   // K and V tiles are read once: let them leave L2 first, so that the kernel's
   // code, the plan inputs, q and the merge partials stay cached.
   const uint64_t kv_policy = l2_evict_first_policy();
@@ -489,15 +498,24 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
 }
 
 
-// At the very end, if counting the first piece completed its unit (the other
-// part finished first), the whole CTA merges the unit's partials.
-__device__ __noinline__ void finish_first_unit(const Ctx& c) {
-  FirstSplit fs;
-  fs.init(c);
+// At the very end, the whole CTA merges the partials of the units its counts
+// completed: the first piece's (its other parts finished first) and the last
+// piece's (its count came last).
+__device__ __noinline__ void finish_units(const Ctx& c) {
+  const VerifyShared* sh = c.sh;
   __threadfence();
-  const int first_row = c.ps.gfirst[fs.g];
-  merge_unit_threads(*c.p, first_row, c.ps.gfirst[fs.g + 1] - first_row, fs.h, c.gqa, fs.w0, fs.w1, threadIdx.x,
-                     kVThreads);
+  if (sh->first_last) {
+    FirstSplit fs;
+    fs.init(c);
+    const int first_row = c.ps.gfirst[fs.g];
+    merge_unit_threads<2>(*c.p, first_row, c.ps.gfirst[fs.g + 1] - first_row, fs.h, c.gqa, fs.w0, fs.w1,
+                          threadIdx.x, kVThreads);
+  }
+  if (sh->last_merge) {
+    const int first_row = c.ps.gfirst[sh->lm_g];
+    merge_unit_threads<2>(*c.p, first_row, c.ps.gfirst[sh->lm_g + 1] - first_row, sh->lm_h, c.gqa, sh->lm_w0,
+                          sh->lm_w1, threadIdx.x, kVThreads);
+  }
 }
 
 // ------------------------------------------------------------------- S issuer
@@ -544,7 +562,6 @@ struct QFeeder {
 __device__ __noinline__ void s_issuer(const Ctx& c, const CUtensorMap* tmap_q) {
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
-  tma_prefetch_desc(tmap_q);
   const uint32_t q_base = smem_u32(c.smem + kQOff);
   const uint32_t k_base = smem_u32(c.smem + kKOff);
   const uint32_t tmem = c.tmem;
@@ -615,11 +632,14 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
   bool ok = true;
   for (int piece = 0; ok && cur.next(g, h, lo, hi, nb, ustart); ++piece) {
     const int nst = stages_of(lo, hi);
+    const int ob = piece & 1;
+    const uint32_t ocol = tmem + kOCol + 128u * ob;
     for (int s = 0; s < nst; ++s, ++G) {
       const int slot = (G / kSlotStages) % kVRing, sb = G & 1;
+      // O buffer ob is free once the epilogue of piece - 2 has read it.
       if (!wait_or_abort(sh, p, &sh->p_full[sb], (uint32_t)((G >> 1) & 1)) ||
           !wait_or_abort(sh, p, &sh->v_full[slot], (uint32_t)((G / kSlotStages / kVRing) & 1)) ||
-          (s == 0 && piece > 0 && !wait_or_abort(sh, p, &sh->o_empty, (uint32_t)((piece - 1) & 1)))) {
+          (s == 0 && piece >= 2 && !wait_or_abort(sh, p, &sh->o_empty[ob], (uint32_t)(((piece - 2) >> 1) & 1)))) {
         ok = false;
         break;
       }
@@ -633,11 +653,12 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
         if (kb < nblk) {
           const uint64_t a = pa0 + (((kb >> 2) * kPAtom + (kb & 3) * 32) >> 4);
           const uint32_t acc = (s == 0 && kb == 0) ? 0u : 1u;
-          mma_f16(tmem + kOCol, a, vb0 + ((kb * 2048) >> 4), idesc_pv, acc);
+          mma_f16(ocol, a, vb0 + ((kb * 2048) >> 4), idesc_pv, acc);
         }
       }
       mma_commit(&sh->v_empty[slot]);
       mma_commit(&sh->pv_done[sb]);
+      if (s == nst - 1) mma_commit(&sh->o_full[ob]);
     }
   }
   mma_commit(&sh->pv_final);
@@ -646,11 +667,11 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
 
 // -------------------------------------------------------------------- softmax
 // O times (alpha_a, alpha_b), in TMEM (rare: a row's max grew by more than 2^8).
-__device__ __noinline__ void rescale_o(uint32_t tmem, uint32_t lane_addr, float alpha_a, float alpha_b) {
+__device__ __noinline__ void rescale_o(uint32_t ocol, uint32_t lane_addr, float alpha_a, float alpha_b) {
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     uint32_t orr[32];
-    const uint32_t oaddr = tmem + kOCol + half * 64 + lane_addr;
+    const uint32_t oaddr = ocol + half * 64 + lane_addr;
     tmem_ld_16x256b_x8(oaddr, orr);
     tmem_wait_ld();
     scale_rows(orr, 8, alpha_a, alpha_b);
@@ -659,26 +680,29 @@ __device__ __noinline__ void rescale_o(uint32_t tmem, uint32_t lane_addr, float 
   tmem_wait_st();
 }
 
-// The rows this thread owns in the current piece and their running state.
+// The rows a softmax or epilogue thread owns in a piece (the two warps of
+// one TMEM lane quadrant own the same rows).
 struct SoftmaxRows {
   int g, h, lo, hi, nb;
   long long ustart;
   int ja, jb, len_a, len_b;  // unit rows (-1: none) and their lengths
 };
 
-// End of a piece: O / l as fp16 output rows, or, for a unit split across
-// CTAs, a partial (O / l and m + log2 l).  The last piece of the CTA's range
-// first looks at the unit's counter: when the one other piece has been counted
-// in already, it merges that partial with its own O directly.  Otherwise it
-// writes its partial and counts it in, and if that completes the unit the
-// softmax warps merge the partials.  The first piece's partial is counted in
-// by the K warp.  The PV issuer may reuse O once it has been read.
-__device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, int G_last, float m_a, float m_b,
+// Epilogue of piece `piece` (run by the epilogue warps while the softmax warps
+// go on with the next piece): O / l as fp16 output rows, or, for a unit split
+// across CTAs, a partial (O / l and m + log2 l).  m and l are the rows' final
+// max and sum.  The last piece of the CTA's range first looks at the unit's
+// counter: when the one other piece has been counted in already, it merges
+// that partial with its own O directly.  Otherwise it writes its partial and
+// counts it in, and if that completes the unit the epilogue warps merge the
+// partials.  The first piece's partial is counted in by the K warp.  The PV
+// issuer may reuse the piece's O buffer once it has been read.
+__device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, int piece, float m_a, float m_b,
                                             float l_a, float l_b, bool last_piece) {
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tid = threadIdx.x - kSoftmaxWarp0 * 32;
+  const int tid = threadIdx.x - kEpiWarp0 * 32;
   const int q4 = lane & 3;
   const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
   const int gqa = c.gqa;
@@ -694,25 +718,21 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
     // The counter is read while the last P V still runs.
     if (last_piece && w1 - w0 <= kMaxDirectOthers) {
       if (tid == 0) sh->merge_mode = ld_acquire_gpu(p.counters + unit) == (int)(w1 - w0);
-      named_bar_sync(2, kSoftmaxThreads);
+      named_bar_sync(2, kEpiThreads);
       direct = sh->merge_mode != 0;
     }
   }
-  if (!wait_or_abort(sh, p, &sh->pv_done[G_last & 1], (uint32_t)((G_last >> 1) & 1))) return false;
+  const int ob = piece & 1;
+  if (!wait_or_abort(sh, p, &sh->o_full[ob], (uint32_t)((piece >> 1) & 1))) return false;
   tc_fence_after();
-  // Row sums: each of a row's four threads holds the sum of its columns.
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     uint32_t o[32];
-    tmem_ld_16x256b_x8(c.tmem + kOCol + half * 64 + lane_addr, o);
+    tmem_ld_16x256b_x8(c.tmem + kOCol + 128u * ob + half * 64 + lane_addr, o);
     tmem_wait_ld();
     if (half == 1) {
       tc_fence_before();
-      warp_arrive(&sh->o_empty);
+      warp_arrive(&sh->o_empty[ob]);
     }
 #pragma unroll 1
     for (int x = 0; x < 2; ++x) {
@@ -797,17 +817,18 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
     } else if (!last_piece) {
       warp_arrive(&sh->part_ready);  // the K warp counts it in
     } else {
-      named_bar_sync(2, kSoftmaxThreads);  // every partial store precedes thread 0's fence
+      named_bar_sync(2, kEpiThreads);  // every partial store precedes thread 0's fence
       if (tid == 0) {
         __threadfence();
-        const int last = atomicAdd(p.counters + unit, 1) == (int)(w1 - w0);
-        if (last) p.counters[unit] = 0;
-        sh->merge_mode = last;
-      }
-      named_bar_sync(2, kSoftmaxThreads);
-      if (sh->merge_mode) {
-        __threadfence();
-        merge_unit_threads(p, first_row, c.ps.gfirst[r.g + 1] - first_row, r.h, gqa, w0, w1, tid, kSoftmaxThreads);
+        // Completing the unit: the whole CTA merges it once every role is done.
+        if (atomicAdd(p.counters + unit, 1) == (int)(w1 - w0)) {
+          p.counters[unit] = 0;
+          sh->lm_g = r.g;
+          sh->lm_h = r.h;
+          sh->lm_w0 = w0;
+          sh->lm_w1 = w1;
+          sh->last_merge = 1;
+        }
       }
     }
   }
@@ -932,10 +953,12 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
   };
   SoftmaxRows cr, nr;
   bool have = fill(cr);
-  int G = 0;
+  int G = 0, piece = 0;
   bool ok = true;
+  float2* stats = reinterpret_cast<float2*>(smem + kStatOff);
   while (have && ok) {
     const bool have_next = fill(nr);
+    const uint32_t ocol = tmem + kOCol + 128u * (piece & 1);
     const bool has_b = __any_sync(0xffffffffu, cr.jb >= 0);  // warp-uniform
     float m_a = neg_inf(), m_b = neg_inf();
     float ls[2] = {0.f, 0.f};  // this thread's part of the row sums
@@ -1012,7 +1035,7 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
           break;
         }
         tc_fence_after();
-        rescale_o(tmem, lane_addr, alpha_a, alpha_b);
+        rescale_o(ocol, lane_addr, alpha_a, alpha_b);
       }
       uint8_t* pbuf = smem + kPOff + sb * kPBuf;
       const float ms[2] = {m_a, m_b};
@@ -1026,9 +1049,49 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
       warp_arrive(&sh->p_full[sb]);
     }
     if (!ok) break;
-    if (!piece_epilogue(c, cr, G - 1, m_a, m_b, ls[0], ls[1], !have_next)) break;
+    // Hand the rows' max and sum (each of a row's four threads holds the sum
+    // of its columns) to the epilogue warps and go on with the next piece.
+    ls[0] += __shfl_xor_sync(0xffffffffu, ls[0], 1);
+    ls[0] += __shfl_xor_sync(0xffffffffu, ls[0], 2);
+    ls[1] += __shfl_xor_sync(0xffffffffu, ls[1], 1);
+    ls[1] += __shfl_xor_sync(0xffffffffu, ls[1], 2);
+    const int b = piece & 1;
+    if (piece >= 2 && !wait_or_abort(sh, p, &sh->st_empty[b], (uint32_t)(((piece - 2) >> 1) & 1))) break;
+    if (q4 == 0) {
+      stats[b * kMaxQRows + ma] = make_float2(m_a, ls[0]);
+      stats[b * kMaxQRows + mb] = make_float2(m_b, ls[1]);
+    }
+    warp_arrive(&sh->st_full[b]);
+    ++piece;
     have = have_next;
     cr = nr;
+  }
+}
+
+// ------------------------------------------------------------------- epilogue
+// Warps kEpiWarp0.. (lane quadrant warp % 4, the rows of the softmax warp of
+// the same quadrant): per piece, the rows' statistics from the softmax, then
+// piece_epilogue on the piece's O buffer.
+__device__ __noinline__ void epilogue_role(const Ctx& c) {
+  VerifyShared* sh = c.sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qd = warp & 3;
+  const int li_a = lane >> 2, li_b = li_a + 8;
+  const int ma = 16 * qd + li_a, mb = ma + 8;
+  const float2* stats = reinterpret_cast<const float2*>(c.smem + kStatOff);
+  PieceCursor cur;
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  SoftmaxRows r;
+  for (int piece = 0; cur.next(r.g, r.h, r.lo, r.hi, r.nb, r.ustart); ++piece) {
+    const int nrows = c.ps.gfirst[r.g + 1] - c.ps.gfirst[r.g];
+    const int cq = c.gqa * rows_per_quad(nrows), nq = nrows * c.gqa;
+    r.ja = (li_a < cq && qd * cq + li_a < nq) ? qd * cq + li_a : -1;
+    r.jb = (li_b < cq && qd * cq + li_b < nq) ? qd * cq + li_b : -1;
+    const int b = piece & 1;
+    if (!wait_or_abort(sh, *c.p, &sh->st_full[b], (uint32_t)((piece >> 1) & 1))) return;
+    const float2 sa = stats[b * kMaxQRows + ma], sbv = stats[b * kMaxQRows + mb];
+    warp_arrive(&sh->st_empty[b]);
+    if (!piece_epilogue(c, r, piece, sa.x, sbv.x, sa.y, sbv.y, cur.t >= cur.t_end)) return;
   }
 }
 
@@ -1048,31 +1111,8 @@ __global__ void __launch_bounds__(kVThreads, 1)
   c.smem = smem;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   grid_launch_dependents();
-  grid_dependency_wait();  // inputs may come from the previous launch in the stream
-  c.ps = PlanSmem{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1),
-                  plan_mem + 2 * (p.num_rows + 1) + 8};
-  build_plan(c.ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, p.max_group_rows);
-  c.ng = c.ps.misc[0];
-  c.hk = p.num_kv_heads;
-  c.gqa = p.num_q_heads / p.num_kv_heads;
-  c.oob_row = args.oob_row;
-  c.total = (long long)c.hk * c.ps.gprefix[c.ng];
-  const long long launched = gridDim.x;
-  c.w = blockIdx.x;
-  if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4)
-    write_nan_rows(p, c.ps, c.ng, c.w * 4 + (warp - kSoftmaxWarp0), launched * 4);
-  if (c.total == 0) return;
-  c.split.gprefix = c.ps.gprefix;
-  c.split.ng = c.ng;
-  c.split.hk = c.hk;
-  c.split.pc = kPieceCost;
-  c.split.vtotal = c.total + (long long)kPieceCost * c.hk * c.ng;
-  c.workers = launched < c.split.vtotal ? launched : c.split.vtotal;
-  c.split.workers = c.workers;
-  if (c.w >= c.workers) return;
-  c.t_begin = c.split.begin(c.w);
-  c.t_end = c.split.begin(c.w + 1);
-
+  // Set-up that reads no input runs before the wait for the previous launch
+  // in the stream, overlapping its tail: barriers, tensor memory, descriptors.
   if (threadIdx.x == 0) {
     for (int i = 0; i < kKRing; ++i) {
       mbar_init(&sh->k_full[i], 1);
@@ -1092,10 +1132,14 @@ __global__ void __launch_bounds__(kVThreads, 1)
       mbar_init(&sh->pv_done[i], 1);
       mbar_init(&sh->q_full[i], 1);
       mbar_init(&sh->q_empty[i], 1);
+      mbar_init(&sh->o_full[i], 1);
+      mbar_init(&sh->o_empty[i], 4);
+      mbar_init(&sh->st_full[i], 4);
+      mbar_init(&sh->st_empty[i], 4);
     }
-    mbar_init(&sh->o_empty, 4);
     mbar_init(&sh->part_ready, 4);
     sh->first_last = 0;
+    sh->last_merge = 0;
     mbar_init(&sh->s_final, 1);
     mbar_init(&sh->pv_final, 1);
     sh->abort_flag = 0;
@@ -1105,13 +1149,46 @@ __global__ void __launch_bounds__(kVThreads, 1)
     tmem_alloc(&sh->tmem_base, kTmemCols);
     tmem_relinquish();
   }
+  if (warp == kKWarp && lane == 0) {
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+    tma_prefetch_desc(&tmap_q);
+  }
+  grid_dependency_wait();  // inputs may come from the previous launch in the stream
+  c.ps = PlanSmem{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1),
+                  plan_mem + 2 * (p.num_rows + 1) + 8};
+  build_plan(c.ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, p.max_group_rows);
+  c.ng = c.ps.misc[0];
+  c.hk = p.num_kv_heads;
+  c.gqa = p.num_q_heads / p.num_kv_heads;
+  c.oob_row = args.oob_row;
+  c.total = (long long)c.hk * c.ps.gprefix[c.ng];
+  const long long launched = gridDim.x;
+  c.w = blockIdx.x;
+  if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4)
+    write_nan_rows(p, c.ps, c.ng, c.w * 4 + (warp - kSoftmaxWarp0), launched * 4);
+  c.split.gprefix = c.ps.gprefix;
+  c.split.ng = c.ng;
+  c.split.hk = c.hk;
+  c.split.pc = kPieceCost;
+  c.split.vtotal = c.total + (long long)kPieceCost * c.hk * c.ng;
+  c.workers = launched < c.split.vtotal ? launched : c.split.vtotal;
+  c.split.workers = c.workers;
   // The roles read the context from shared memory (one copy per CTA) rather
   // than from a stack copy per thread, which would live in local memory.
   if (threadIdx.x == 0) sh->ctx = c;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (threadIdx.x == 0) sh->ctx.tmem = sh->tmem_base;
+  if (c.total == 0 || c.w >= c.workers) {  // no tiles for this CTA (uniform over the CTA)
+    if (warp == kSWarp) tmem_dealloc(sh->tmem_base, kTmemCols);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    sh->ctx.t_begin = c.split.begin(c.w);
+    sh->ctx.t_end = c.split.begin(c.w + 1);
+    sh->ctx.tmem = sh->tmem_base;
+  }
   __syncthreads();
   const Ctx& cs = sh->ctx;
 
@@ -1125,6 +1202,8 @@ __global__ void __launch_bounds__(kVThreads, 1)
     if (lane == 0) s_issuer(cs, &tmap_q);
   } else if (warp == kPVWarp) {
     if (lane == 0) pv_issuer(cs);
+  } else if (warp >= kEpiWarp0) {
+    epilogue_role(cs);
   } else {
     softmax_role(cs);
   }
@@ -1132,7 +1211,7 @@ __global__ void __launch_bounds__(kVThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == kSWarp) tmem_dealloc(cs.tmem, kTmemCols);
-  if (!aborted(sh) && sh->first_last) finish_first_unit(cs);
+  if (!aborted(sh) && (sh->first_last || sh->last_merge)) finish_units(cs);
 }
 
 // ------------------------------------------------------------------ host side
