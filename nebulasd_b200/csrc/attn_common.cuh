@@ -33,16 +33,39 @@ struct AttnParams {
   float* part_o;      // [2 * workers][nq][128]
   int32_t nq;         // partial rows per slot = gqa * max_group_rows
   int32_t max_group_rows;
+  int32_t* plan_cache;  // two plan-cache slots (verify kernel)
 };
 
-// Workspace: header | counters | part_lse | part_o, each 256-byte aligned.
-// The counter region has a fixed size and place whatever the call's shape, so
-// the partials of one call can never land where a later call (with more rows
-// or heads) keeps counters that must read zero.
+// Workspace: header | counters | plan cache | part_lse | part_o, each 256-byte
+// aligned.  The counter region has a fixed size and place whatever the call's
+// shape, so the partials of one call can never land where a later call (with
+// more rows or heads) keeps counters that must read zero; the plan cache too.
 constexpr int kMaxKvHeads = 64;
 
+// Plan cache of the verify kernel: the work plan depends only on the rows'
+// seq ids and lengths and the call's shape, which the 36 layer calls of one
+// forward share.  A call with launch number n (counted per workspace on the
+// host) reads slot (n + 1) % 2, written by call n - 1, and writes slot n % 2;
+// a slot is used only when its key, the row arrays and the CTA's own entry
+// all match, so a stale or foreign slot just means the plan is rebuilt.
+// Slot, in 32-bit words: key [16] | seq ids [kMaxRows] | lengths [kMaxRows] |
+// plan arrays as laid out in shared memory [3 * (kMaxRows + 1) + 8] | per
+// worker [kPcEntryWords]: {seq, first group, t_begin, t_end} and, from word
+// kPcEntryFeed, the block-table entries of its first 96 tiles (64-bit each).
+constexpr int kPlanCacheWorkers = 256;
+constexpr uint32_t kPlanCacheMagic = 0x4e504331u;
+constexpr int kPcIds = 16;
+constexpr int kPcLens = kPcIds + kMaxRows;
+constexpr int kPcPlan = kPcLens + kMaxRows;
+constexpr int kPcWorkers = (kPcPlan + 3 * (kMaxRows + 1) + 8 + 7) & ~7;
+constexpr int kPcEntryFeed = 8;
+constexpr int kPcEntryWords = 256;
+constexpr int kPcSlotWords = ((kPcWorkers + kPlanCacheWorkers * kPcEntryWords) + 63) & ~63;
+static_assert(kPcEntryFeed + 2 * 96 <= kPcEntryWords, "a worker's entry holds its 96 tile words");
+constexpr size_t kPlanCacheBytes = 2ull * kPcSlotWords * sizeof(int32_t);
+
 struct WorkspaceLayout {
-  size_t counters, part_lse, part_o, total;
+  size_t counters, plan_cache, part_lse, part_o, total;
 };
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -53,7 +76,8 @@ __host__ __device__ inline WorkspaceLayout workspace_layout(long long workers, i
   (void)num_kv_heads;
   WorkspaceLayout L;
   L.counters = sizeof(WorkspaceHeader);
-  L.part_lse = L.counters + align256((size_t)kMaxRows * kMaxKvHeads * sizeof(int32_t));
+  L.plan_cache = L.counters + align256((size_t)kMaxRows * kMaxKvHeads * sizeof(int32_t));
+  L.part_lse = L.plan_cache + align256(kPlanCacheBytes);
   L.part_o = L.part_lse + align256((size_t)2 * workers * nq * sizeof(float));
   L.total = L.part_o + align256((size_t)2 * workers * nq * kHeadDim * sizeof(float));
   return L;

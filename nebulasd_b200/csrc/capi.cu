@@ -105,6 +105,7 @@ static int bind_workspace(AttnParams& p, void* workspace, size_t workspace_bytes
   p.counters = reinterpret_cast<int32_t*>(base + L.counters);
   p.part_lse = reinterpret_cast<float*>(base + L.part_lse);
   p.part_o = reinterpret_cast<float*>(base + L.part_o);
+  p.plan_cache = reinterpret_cast<int32_t*>(base + L.plan_cache);
   p.nq = nq;
   return NEB_OK;
 }
@@ -250,7 +251,7 @@ static int read_and_clear_status(void* base, uint32_t* error_bits, cudaStream_t 
     NEB_CUDA(cudaMemsetAsync(base, 0, sizeof(uint32_t), s));
     if (h.error_bits & kErrTimeout) {
       const WorkspaceLayout L = workspace_layout(1, 1, 1, 1);
-      NEB_CUDA(cudaMemsetAsync(static_cast<char*>(base) + L.counters, 0, L.part_lse - L.counters, s));
+      NEB_CUDA(cudaMemsetAsync(static_cast<char*>(base) + L.counters, 0, L.plan_cache - L.counters, s));
     }
     NEB_CUDA(cudaStreamSynchronize(s));
   }

@@ -135,6 +135,83 @@ static __device__ __noinline__ void build_plan(PlanSmem ps, int* scratch, const 
   __syncthreads();
 }
 
+// The same plan built by one warp (all 32 lanes call it; no block barrier), so
+// that the rest of the CTA can be released by an mbarrier as soon as it is in
+// shared memory.  Rows go 32 at a time, one per lane: a run of one seq_id
+// starts where the id changes (ballot), a group starts there or every
+// max_group_rows rows into the run, and group indices come from popcounts.
+// Up to four chunks' loads are in flight before the first is used.
+static __device__ __noinline__ void build_plan_warp(PlanSmem ps, const int32_t* __restrict__ seq_ids,
+                                                    const int32_t* __restrict__ seq_lens, int num_rows,
+                                                    int max_group_rows) {
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u, le = lt | (1u << lane);
+  int run = 0, groups = 0, last_sid = 0;
+  for (int base = 0; base < num_rows; base += 128) {
+    int sid[4], len[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int r = base + 32 * k + lane;
+      sid[k] = r < num_rows ? __ldg(seq_ids + r) : 0;
+      len[k] = r < num_rows ? __ldg(seq_lens + r) : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int b = base + 32 * k;
+      if (b >= num_rows) break;
+      const int r = b + lane;
+      const bool valid = r < num_rows;
+      int prev = __shfl_up_sync(0xffffffffu, sid[k], 1);
+      if (lane == 0) prev = last_sid;
+      const bool seq_start = valid && (r == 0 || sid[k] != prev);
+      const unsigned runs = __ballot_sync(0xffffffffu, seq_start) & le;
+      const int run_start = runs ? b + 31 - __clz(runs) : run;
+      const bool gstart = valid && (seq_start || (r - run_start) % max_group_rows == 0);
+      const unsigned gb = __ballot_sync(0xffffffffu, gstart);
+      if (gstart) {
+        const int gidx = groups + __popc(gb & lt);
+        ps.gfirst[gidx] = r;
+        if (ps.gsid) ps.gsid[gidx] = sid[k];
+      }
+      if (valid) ps.gprefix[r] = len[k];  // row lengths, read back below
+      run = __shfl_sync(0xffffffffu, run_start, 31);
+      last_sid = __shfl_sync(0xffffffffu, sid[k], 31);
+      groups += __popc(gb);
+    }
+  }
+  const int ng = groups;
+  if (lane == 0) {
+    ps.gfirst[ng] = num_rows;
+    ps.misc[0] = ng;
+  }
+  __syncwarp();
+  // Tiles per group (max length over its rows) and their exclusive prefix.
+  // A chunk reads lengths of rows >= its first group before writing
+  // gprefix[g] for its own groups (< the rows of later chunks).
+  int carry = 0;
+  for (int gb0 = 0; gb0 < ng; gb0 += 32) {
+    const int g = gb0 + lane;
+    int nb = 0;
+    if (g < ng) {
+      int mx = 0;
+      for (int r = ps.gfirst[g]; r < ps.gfirst[g + 1]; ++r) mx = max(mx, ps.gprefix[r]);
+      nb = (mx + 15) >> 4;
+    }
+    int incl = nb;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    __syncwarp();
+    if (g < ng) ps.gprefix[g] = carry + incl - nb;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();
+  }
+  if (lane == 0) ps.gprefix[ng] = carry;
+  __syncwarp();
+}
+
 // Largest group g with hk * gprefix[g] <= t (t < hk * gprefix[ng]); skips empty groups.
 __device__ __forceinline__ int find_group(const int* gprefix, int ng, long long t, int hk) {
   int lo = 0, hi = ng;  // invariant: hk*gprefix[lo] <= t < hk*gprefix[hi]

@@ -56,6 +56,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <unordered_map>
 
 #include "attn_common.cuh"
 #include "sm100.cuh"
@@ -72,26 +73,26 @@ constexpr int kEpiWarp0 = 8;                              // epilogue warps: TME
 constexpr int kEpiThreads = 128;
 constexpr int kVWarp = 6;
 constexpr int kPVWarp = 7;
-constexpr int kStageBlocks = 4;                           // 16-token KV blocks per stage
+constexpr int kStageBlocks = 8;                           // 16-token KV blocks per stage
 constexpr int kStageCols = kStageBlocks * kBlockTokens;   // tokens per stage: the S tile's N
 constexpr int kStageR = kStageCols / 8;                   // 8-column groups of an S tile
-constexpr int kSlotStages = 2;                            // stages per K (V) ring slot: one TMA phase
+constexpr int kSlotStages = 1;                            // stages per K (V) ring slot: one TMA phase
 constexpr int kKRing = 2;                                 // slots of the K ring
 constexpr int kVRing = 2;                                 // slots of the V ring
-constexpr int kSBufs = 4;                                 // S tiles in TMEM (the S issuer runs ahead)
+constexpr int kSBufs = 2;                                 // S tiles in TMEM (the S issuer runs ahead)
 constexpr int kFlagSlots = kSlotStages * kKRing + kSBufs;  // block-flag ring (see the K producer)
 constexpr int kMaxQRows = 64;                             // query rows per unit: the MMA's M
 constexpr int kMaxGqa = 16;                               // a row's heads fit one 16-row chunk
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSBuf = 64;                            // S tile b at columns 64*b
+constexpr uint32_t kSBuf = 128;                           // S tile b at columns 128*b
 constexpr uint32_t kOCol = 256;                           // O of piece i: 128 columns at kOCol + 128 * (i % 2)
 constexpr long long kWaitLimit = 4000000000LL;
 constexpr int kMaxDirectOthers = 3;                      // direct merge: at most 3 other pieces
 constexpr int kPieceCost = 8;                             // a piece's fixed cost, in tiles (plan.cuh CostSplit)
 static_assert(kStageCols <= (int)kSBuf && kStageR % 2 == 0 && kSBufs * kSBuf <= kOCol && kOCol + 256 <= kTmemCols,
               "S tiles and both O buffers fit TMEM");
-static_assert(kSlotStages == 2 && (kStageBlocks & (kStageBlocks - 1)) == 0 && 2 * kSlotStages * kStageBlocks <= 32,
-              "the producers fill a slot with two stages, one 64-column box per lane");
+static_assert(kSlotStages == 1 && kStageBlocks == 8 && 2 * kSlotStages * kStageBlocks <= 32,
+              "the producers fill a slot with one stage, one 64-column box per lane");
 
 // Shared memory map (offsets from a 1024-byte aligned base).
 constexpr uint32_t kQHalf = kMaxQRows * 128;       // one 64-column half of Q
@@ -106,7 +107,8 @@ constexpr uint32_t kPAtom = kMaxQRows * 128;       // 64 rows x 64 fp16 of P (on
 constexpr uint32_t kPBuf = ((kStageCols + 63) / 64) * kPAtom;
 constexpr uint32_t kPOff = kVOff + kVRing * kSlotBytes;
 constexpr uint32_t kStatOff = kPOff + 2 * kPBuf;   // row max and sum of a piece: [2][64] float2
-constexpr uint32_t kBarOff = kStatOff + 2 * kMaxQRows * 8;
+constexpr uint32_t kFeedOff = kStatOff + 2 * kMaxQRows * 8;  // the first 96 tiles' table entries (plan cache)
+constexpr uint32_t kBarOff = kFeedOff + 1024;
 constexpr uint32_t kPlanOff = kBarOff + 1024;
 static_assert(kHalf % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 
@@ -127,10 +129,15 @@ struct Ctx {
   long long total, workers, w, t_begin, t_end;
   CostSplit split;  // which worker owns which tiles
   uint32_t tmem;
+  int g_begin;          // group of tile t_begin
+  bool pc_hit;          // the plan came from the plan cache (and so did feed_cache)
+  uint32_t seq;         // launch number (plan cache)
+  int32_t* pc_entry;    // this worker's entry in the slot written for the next call (null: none)
 };
 
 struct VerifyShared {
-  Ctx ctx;                       // the launch context, written once by thread 0
+  AttnParams prm;                // the call's parameters, copied in before the inputs are read
+  Ctx ctx;                       // the launch context, written once by warp 0
   uint64_t k_full[kKRing];       // K of the slot's stages landed
   uint64_t k_empty[kKRing];      // S of the slot's stages completed (one arrival per stage)
   uint64_t v_full[kVRing];       // V of the slot's stages landed
@@ -146,12 +153,15 @@ struct VerifyShared {
   uint64_t o_empty[2];           // the epilogue read O buffer i % 2 (one arrival per epilogue warp)
   uint64_t st_full[2];           // the softmax wrote piece i's row statistics (one arrival per warp)
   uint64_t st_empty[2];          // the epilogue read them
+  uint64_t plan_ready;           // warp 0 wrote the plan and the context
   uint64_t part_ready;           // softmax wrote the partial of the CTA's first piece (split, not last)
   uint64_t s_final;
   uint64_t pv_final;
   uint32_t tmem_base;
   int32_t abort_flag;
   int32_t merge_mode;            // epilogue of the last piece: merge directly with the other partial
+  long long cached_begin, cached_end;  // this worker's tile range from the plan cache
+  int32_t cached_group;          // and the group of its first tile
   int32_t first_last;            // the first piece's count completed its unit: merge it at the end
   int32_t last_merge;            // the last piece's count completed its unit: merge it at the end
   int32_t lm_g, lm_h;            // that unit's group and kv head
@@ -166,7 +176,8 @@ __host__ __device__ inline size_t verify_smem_bytes(int num_rows) {
 
 struct VerifyArgs {
   AttnParams p;
-  int oob_row;  // first row past the end of the K/V tensor maps (loads there return zeros)
+  int oob_row;   // first row past the end of the K/V tensor maps (loads there return zeros)
+  uint32_t seq;  // launch number on this workspace (plan cache slots)
 };
 
 
@@ -175,13 +186,15 @@ struct PieceCursor {
   const PlanSmem* ps;
   int ng, hk, g;
   long long t, t_end;
-  __device__ __noinline__ void init(const PlanSmem* planp, int ngroups, int kvh, long long begin, long long end) {
+  // g0: the group of tile `begin` when known, else -1.
+  __device__ __noinline__ void init(const PlanSmem* planp, int ngroups, int kvh, long long begin, long long end,
+                                    int g0 = -1) {
     ps = planp;
     ng = ngroups;
     hk = kvh;
     t = begin;
     t_end = end;
-    g = begin < end ? find_group(ps->gprefix, ng, begin, hk) : 0;
+    g = begin >= end ? 0 : g0 >= 0 ? g0 : find_group(ps->gprefix, ng, begin, hk);
   }
   // Fills (group, kv_head, tile_lo, tile_hi, nb, unit_start); false when done.
   __device__ __forceinline__ bool next(int& grp, int& kv_head, int& lo, int& hi, int& nb, long long& unit_start) {
@@ -305,45 +318,51 @@ struct TileFeed {
     }
   }
   __device__ __forceinline__ void fetch(long long bt, int& r, int& v) const { resolve(locate(bt), r, v); }
-  // resolve() in three parts, so that several tiles' table reads are in
-  // flight together: no error is recorded (an atomic) between the loads.
-  __device__ __forceinline__ long long table_pos(const Pending& q, uint32_t& err) const {
+  // A lane's tile as one word: its block-table position times 256 plus its
+  // kv head, -1 for no table entry, -2 for a tile past max_blocks_per_seq.
+  // The first three batches' words are what the plan cache keeps per worker.
+  __device__ __forceinline__ long long entry(const Pending& q) const {
     if (!q.in_range || q.sid < 0 || q.sid >= p->bt_rows) return -1;
-    if (q.tile >= p->mbs) {
-      err |= kErrTooManyBlocks;
-      return -1;
-    }
-    return (long long)q.sid * p->mbs + q.tile;
+    if (q.tile >= p->mbs) return -2;
+    return (((long long)q.sid * p->mbs + q.tile) << 8) | q.kv_head;
   }
-  __device__ __forceinline__ void finish(const Pending& q, long long pos, long long blk, uint32_t& err, int& r,
-                                         int& v) const {
+  __device__ __forceinline__ void finish_entry(long long e, long long blk, uint32_t& err, int& r, int& v) const {
     r = oob_row;
     v = 0;
-    if (pos < 0) return;  // no table entry read
+    if (e == -2) err |= kErrTooManyBlocks;
+    if (e < 0) return;
     if (blk < 0 || blk >= p->num_blocks) {
       err |= kErrBlockIndex;
       return;
     }
     v = 1;
-    r = (int)(((blk * p->num_layers + p->cur_layer) * p->num_kv_heads + q.kv_head) * kBlockTokens);
+    r = (int)(((blk * p->num_layers + p->cur_layer) * p->num_kv_heads + (int)(e & 255)) * kBlockTokens);
   }
+  // The first three batches, from the words in `cached` ([3][32], as left by
+  // an earlier call) or located here; `e` returns this lane's words.
   __device__ void init(const AttnParams* pp, const PlanSmem* pps, int ngroups, int oob, long long begin,
-                       long long end) {
+                       long long end, const long long* cached, long long* e) {
     p = pp;
     ps = pps;
     ng = ngroups;
     oob_row = oob;
     t_end = end;
     base = begin;
-    const Pending q0 = locate(base), q1 = locate(base + 32), q2 = locate(base + 64);
+    const int lane = threadIdx.x & 31;
+    if (cached) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) e[k] = cached[32 * k + lane];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) e[k] = entry(locate(base + 32 * k));
+    }
     uint32_t err = 0;
-    const long long i0 = table_pos(q0, err), i1 = table_pos(q1, err), i2 = table_pos(q2, err);
-    const long long b0 = i0 >= 0 ? (long long)__ldg(p->block_table + i0) : 0;
-    const long long b1 = i1 >= 0 ? (long long)__ldg(p->block_table + i1) : 0;
-    const long long b2 = i2 >= 0 ? (long long)__ldg(p->block_table + i2) : 0;
-    finish(q0, i0, b0, err, r0, v0);
-    finish(q1, i1, b1, err, r1, v1);
-    finish(q2, i2, b2, err, r2, v2);
+    const long long b0 = e[0] >= 0 ? (long long)__ldg(p->block_table + (e[0] >> 8)) : 0;
+    const long long b1 = e[1] >= 0 ? (long long)__ldg(p->block_table + (e[1] >> 8)) : 0;
+    const long long b2 = e[2] >= 0 ? (long long)__ldg(p->block_table + (e[2] >> 8)) : 0;
+    finish_entry(e[0], b0, err, r0, v0);
+    finish_entry(e[1], b1, err, r1, v1);
+    finish_entry(e[2], b2, err, r2, v2);
     if (err) record_error(*p, err);
   }
   // Row and flag of tile pos + b (b per lane), for base <= pos + b < base + 64.
@@ -375,7 +394,7 @@ struct FirstSplit {
   int g, h;
   __device__ __noinline__ void init(const Ctx& c) {
     PieceCursor cur;
-    cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+    cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end, c.g_begin);
     int lo, hi, nb;
     long long ustart;
     pending = false;
@@ -402,16 +421,16 @@ struct FirstSplit {
 
 // ------------------------------------------------------------------ producers
 // One function serves the K warp (flags != 0: it also publishes the block
-// flags) and the V warp, over a ring of `ring` slots (kKRing, kVRing) of
-// kSlotStages stages each: one TMA phase per slot, so that each wait and
-// transaction count covers 32 KB.  Stage G sits in slot (G / 2) % ring; the
-// slot frees when the MMAs that read its stages (S for K, P V for V) are done.
-// The block flags of stage G go to flag slot G % kFlagSlots.  Before the flags
-// of stages G and G + 1 are written, the slot that held stages G - 2*kKRing and
-// G - 2*kKRing + 1 has been freed, so S of those stages was issued, which
-// needed S buffer (G - 2*kKRing + 1) % kSBufs released by the softmax of stage
-// G - 2*kKRing + 1 - kSBufs, and the softmax reads a stage's flags before it
-// releases its S: flag slots with kFlagSlots >= 2*kKRing + kSBufs are free.
+// flags) and the V warp, over a ring of `ring` slots (kKRing, kVRing) of one
+// 128-token stage each: one TMA phase per slot, so that each wait and
+// transaction count covers 32 KB.  Stage G sits in slot G % ring; the slot
+// frees when the MMAs that read it (S for K, P V for V) are done.  The block
+// flags of stage G go to flag slot G % kFlagSlots.  Before the flags of stage
+// G are written, the slot that held stage G - kKRing has been freed, so S of
+// that stage was issued, which needed S buffer (G - kKRing) % kSBufs released
+// by the softmax of stage G - kKRing - kSBufs, and the softmax reads a stage's
+// flags before it releases its S: flag slots with kFlagSlots >= kKRing +
+// kSBufs are free.
 __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uint64_t* full, uint64_t* empty,
                                       uint32_t ring_off, int ring, int flags, FirstSplit* first) {
   const AttnParams& p = *c.p;
@@ -421,11 +440,12 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
   // code, the plan inputs, q and the merge partials stay cached.
   const uint64_t kv_policy = l2_evict_first_policy();
   TileFeed feed;
-  feed.init(&p, &c.ps, c.ng, c.oob_row, c.t_begin, c.t_end);
+  long long e[3];
+  feed.init(&p, &c.ps, c.ng, c.oob_row, c.t_begin, c.t_end, c.pc_hit ? reinterpret_cast<const long long*>(c.smem + kFeedOff) : nullptr, e);
   // The worker's stages in order, as block counts: each piece cut into
   // kStageBlocks-block stages (the last one of a piece may be shorter).
   PieceCursor cur;
-  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end, c.g_begin);
   int s_lo = 0, s_hi = 0;
   auto next_stage = [&](int& nblk) -> bool {
     if (s_lo >= s_hi) {
@@ -437,57 +457,61 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
     s_lo += nblk;
     return true;
   };
-  // Lane l < 16 carries box (l & 7) of the slot's stage l >> 3: tile l & 3,
-  // half (l >> 2) & 1.
-  const int st = lane >> 3, b = lane & (kStageBlocks - 1), hf = (lane >> 2) & 1;
-  int G = 0, slot = 0, used = 0;  // first stage of the slot, the slot, slots filled so far
+  // Lane l < 16 carries box l of the stage: tile l & 7, half l >> 3.
+  const int b = lane & (kStageBlocks - 1), hf = lane >> 3;
+  int G = 0, slot = 0, used = 0;  // the stage, its slot, slots filled so far
   uint32_t phase = 0;             // parity of the slot's current use
   long long pos = c.t_begin;
   int n0 = 0;
   bool more = next_stage(n0);
   while (more) {
-    int n1 = 0;
-    const bool two = next_stage(n1);
-    const int nst = two ? 2 : 1;
-    const int nb_st = st ? n1 : n0;
     int row, valid;
-    feed.get_lane(pos, (st ? n0 : 0) + b, row, valid);
+    feed.get_lane(pos, b, row, valid);
     int waited = 1;
     if (lane == 0) {
       waited = wait_or_abort(sh, p, &empty[slot], phase ^ 1u);
       if (waited) {
-        mbar_arrive_expect_tx(&full[slot], (uint32_t)(n0 + n1) * 2u * 2048u);
+        mbar_arrive_expect_tx(&full[slot], (uint32_t)n0 * 2u * 2048u);
       }
     }
     waited = __shfl_sync(0xffffffffu, waited, 0);
     if (waited) {
-      // One lane per 64-column box, so that the slot's loads leave together.
-      if (st < nst && b < nb_st)
-        tma_load_2d_hint(c.smem + ring_off + slot * kSlotBytes + st * kStageBytes + hf * kHalf + b * 2048, tmap,
-                         &full[slot], 64 * hf, row, kv_policy);
+      // One lane per 64-column box, so that the stage's loads leave together.
+      if (hf < 2 && b < n0)
+        tma_load_2d_hint(c.smem + ring_off + slot * kSlotBytes + hf * kHalf + b * 2048, tmap, &full[slot], 64 * hf,
+                         row, kv_policy);
       if (flags) {
-        if (st < nst && hf == 0) sh->blk[(G + st) % kFlagSlots][b] = b < nb_st ? valid : 0;
+        if (hf == 0) sh->blk[G % kFlagSlots][b] = b < n0 ? valid : 0;
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sh->flags_full[G % kFlagSlots]);
-          if (two) mbar_arrive(&sh->flags_full[(G + 1) % kFlagSlots]);
-        }
+        if (lane == 0) mbar_arrive(&sh->flags_full[G % kFlagSlots]);
       }
     }
-    // The K warp counts the first piece in as soon as its partial is written
-    // (which piece that is, it works out once the first loads are on their way).
-    if (first && G == 0) first->init(c);
+    // Once the first loads are on their way, the K warp leaves its range for
+    // the next call and works out which piece (if any) it counts in early.
+    if (first && G == 0) {
+      if (c.pc_entry) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) reinterpret_cast<long long*>(c.pc_entry + kPcEntryFeed)[32 * k + lane] = e[k];
+        if (lane == 0) {
+          c.pc_entry[1] = c.g_begin;
+          *reinterpret_cast<long long*>(c.pc_entry + 2) = c.t_begin;
+          *reinterpret_cast<long long*>(c.pc_entry + 4) = c.t_end;
+          c.pc_entry[0] = (int32_t)c.seq;
+        }
+      }
+      first->init(c);
+    }
     if (lane == 0 && first && first->pending && mbar_test_wait(&sh->part_ready, 0)) first->count(c);
     if (!waited) break;
     ++used;
-    pos += n0 + n1;
+    pos += n0;
     feed.advance(pos);
-    G += nst;
+    ++G;
     if (++slot == ring) {
       slot = 0;
       phase ^= 1u;
     }
-    more = two && next_stage(n0);
+    more = next_stage(n0);
   }
   if (lane == 0 && first && first->pending && wait_or_abort(sh, p, &sh->part_ready, 0)) first->count(c);
   // Wait (bounded) for every copy this warp issued before the CTA can exit.
@@ -566,11 +590,11 @@ __device__ __noinline__ void s_issuer(const Ctx& c, const CUtensorMap* tmap_q) {
   const uint32_t k_base = smem_u32(c.smem + kKOff);
   const uint32_t tmem = c.tmem;
   QFeeder qf;
-  qf.cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  qf.cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end, c.g_begin);
   qf.qi = 0;
   qf.qhave = qf.cur.next(qf.qg, qf.qh, qf.qlo, qf.qhi, qf.qnb, qf.qus);
   PieceCursor cur;
-  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end, c.g_begin);
   int g, h, lo, hi, nb;
   long long ustart;
   int G = 0;
@@ -625,7 +649,7 @@ __device__ __noinline__ void pv_issuer(const Ctx& c) {
   const uint32_t idesc_pv = idesc_f16_f32(kMaxQRows, 128, false, true);
   const uint32_t tmem = c.tmem;
   PieceCursor cur;
-  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end, c.g_begin);
   int g, h, lo, hi, nb;
   long long ustart;
   int G = 0;
@@ -937,7 +961,7 @@ __device__ __noinline__ void softmax_role(const Ctx& c) {
   fence_proxy_async_smem();
   named_bar_sync(1, kSoftmaxThreads);
   PieceCursor cur;
-  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end, c.g_begin);
   // Unit rows of this thread in a piece's group, and their lengths (loaded a
   // piece ahead of use).
   auto fill = [&](SoftmaxRows& r) -> bool {
@@ -1080,7 +1104,7 @@ __device__ __noinline__ void epilogue_role(const Ctx& c) {
   const int ma = 16 * qd + li_a, mb = ma + 8;
   const float2* stats = reinterpret_cast<const float2*>(c.smem + kStatOff);
   PieceCursor cur;
-  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end);
+  cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end, c.g_begin);
   SoftmaxRows r;
   for (int piece = 0; cur.next(r.g, r.h, r.lo, r.hi, r.nb, r.ustart); ++piece) {
     const int nrows = c.ps.gfirst[r.g + 1] - c.ps.gfirst[r.g];
@@ -1098,21 +1122,20 @@ __device__ __noinline__ void epilogue_role(const Ctx& c) {
 __global__ void __launch_bounds__(kVThreads, 1)
     verify_attn_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                        const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ VerifyArgs args) {
-  const AttnParams& p = args.p;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   VerifyShared* sh = reinterpret_cast<VerifyShared*>(smem + kBarOff);
+  const AttnParams& p = sh->prm;
   int* plan_mem = reinterpret_cast<int*>(smem + kPlanOff);
-  __shared__ int scratch[32];
-
-  Ctx c;
-  c.p = &p;
-  c.sh = sh;
-  c.smem = smem;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   grid_launch_dependents();
   // Set-up that reads no input runs before the wait for the previous launch
-  // in the stream, overlapping its tail: barriers, tensor memory, descriptors.
+  // in the stream, overlapping its tail: the parameters into shared memory
+  // (the roles read them there, not through first-touch constant-cache
+  // misses), barriers, tensor memory, descriptors.
+  static_assert(sizeof(AttnParams) % 4 == 0 && sizeof(AttnParams) / 4 <= kVThreads, "one word per thread");
+  if (threadIdx.x < sizeof(AttnParams) / 4)
+    reinterpret_cast<uint32_t*>(&sh->prm)[threadIdx.x] = reinterpret_cast<const uint32_t*>(&args.p)[threadIdx.x];
   if (threadIdx.x == 0) {
     for (int i = 0; i < kKRing; ++i) {
       mbar_init(&sh->k_full[i], 1);
@@ -1137,6 +1160,7 @@ __global__ void __launch_bounds__(kVThreads, 1)
       mbar_init(&sh->st_full[i], 4);
       mbar_init(&sh->st_empty[i], 4);
     }
+    mbar_init(&sh->plan_ready, 1);
     mbar_init(&sh->part_ready, 4);
     sh->first_last = 0;
     sh->last_merge = 0;
@@ -1154,45 +1178,143 @@ __global__ void __launch_bounds__(kVThreads, 1)
     tma_prefetch_desc(&tmap_v);
     tma_prefetch_desc(&tmap_q);
   }
-  grid_dependency_wait();  // inputs may come from the previous launch in the stream
-  c.ps = PlanSmem{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1),
-                  plan_mem + 2 * (p.num_rows + 1) + 8};
-  build_plan(c.ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, p.max_group_rows);
-  c.ng = c.ps.misc[0];
-  c.hk = p.num_kv_heads;
-  c.gqa = p.num_q_heads / p.num_kv_heads;
-  c.oob_row = args.oob_row;
-  c.total = (long long)c.hk * c.ps.gprefix[c.ng];
-  const long long launched = gridDim.x;
-  c.w = blockIdx.x;
-  if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4)
-    write_nan_rows(p, c.ps, c.ng, c.w * 4 + (warp - kSoftmaxWarp0), launched * 4);
-  c.split.gprefix = c.ps.gprefix;
-  c.split.ng = c.ng;
-  c.split.hk = c.hk;
-  c.split.pc = kPieceCost;
-  c.split.vtotal = c.total + (long long)kPieceCost * c.hk * c.ng;
-  c.workers = launched < c.split.vtotal ? launched : c.split.vtotal;
-  c.split.workers = c.workers;
-  // The roles read the context from shared memory (one copy per CTA) rather
-  // than from a stack copy per thread, which would live in local memory.
-  if (threadIdx.x == 0) sh->ctx = c;
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // barriers and the tensor-memory address are visible to every thread
   tc_fence_after();
-  if (c.total == 0 || c.w >= c.workers) {  // no tiles for this CTA (uniform over the CTA)
-    if (warp == kSWarp) tmem_dealloc(sh->tmem_base, kTmemCols);
-    return;
+  grid_dependency_wait();  // inputs may come from the previous launch in the stream
+  // The plan of the previous call on this workspace, if it is this call's:
+  // every thread loads a share of it and of the rows' seq ids and lengths in
+  // one round of independent loads, the plan arrays straight into place.
+  const bool cacheable = gridDim.x <= kPlanCacheWorkers && p.num_rows <= kMaxRows;
+  const int32_t* rd = p.plan_cache + (((args.seq & 1u) ^ 1u) * kPcSlotWords);
+  bool same = cacheable;
+  if (cacheable) {
+    // Every load is issued before any comparison (no short-circuit between
+    // loads), so that the whole check costs one memory round trip.
+    for (int i = threadIdx.x; i < p.num_rows; i += kVThreads) {
+      const int a = __ldcg(p.seq_ids + i), b = __ldcg(rd + kPcIds + i);
+      const int c = __ldcg(p.seq_lens + i), d = __ldcg(rd + kPcLens + i);
+      same &= (a == b) & (c == d);
+    }
+    for (int i = threadIdx.x; i < 3 * (p.num_rows + 1) + 8; i += kVThreads) plan_mem[i] = __ldcg(rd + kPcPlan + i);
+    if (threadIdx.x < 32) {
+      // Lanes 0..9: the key; lane 10: this worker's entry; lane 11 its range.
+      const int32_t* wk = rd + kPcWorkers + blockIdx.x * kPcEntryWords;
+      const long long* feed = reinterpret_cast<const long long*>(wk + kPcEntryFeed);
+      const int32_t v = __ldcg(lane < 10 ? rd + lane : wk);
+      const long long range = lane == 11 ? __ldcg(reinterpret_cast<const long long*>(wk + 2)) : 0;
+      const long long range_end = lane == 11 ? __ldcg(reinterpret_cast<const long long*>(wk + 4)) : 0;
+      const int32_t group = lane == 11 ? __ldcg(wk + 1) : 0;
+      const long long f0 = __ldcg(feed + lane), f1 = __ldcg(feed + 32 + lane), f2 = __ldcg(feed + 64 + lane);
+      const int32_t want = lane == 0 ? (int32_t)kPlanCacheMagic
+                         : lane == 1 ? (int32_t)(args.seq - 1u)
+                         : lane == 2 ? p.num_rows
+                         : lane == 3 ? p.max_group_rows
+                         : lane == 4 ? p.num_kv_heads
+                         : lane == 5 ? p.num_q_heads
+                         : lane == 6 ? (int32_t)gridDim.x
+                         : lane == 7 ? kPieceCost
+                         : lane == 8 ? p.mbs
+                         : lane == 9 ? p.bt_rows
+                         : lane == 10 ? (int32_t)(args.seq - 1u) : v;
+      same &= __all_sync(0xffffffffu, v == want);
+      if (lane == 11) {
+        sh->cached_begin = range;
+        sh->cached_end = range_end;
+        sh->cached_group = group;
+      }
+      long long* feed_smem = reinterpret_cast<long long*>(smem + kFeedOff);
+      feed_smem[lane] = f0;
+      feed_smem[32 + lane] = f1;
+      feed_smem[64 + lane] = f2;
+    }
   }
-  if (threadIdx.x == 0) {
-    sh->ctx.t_begin = c.split.begin(c.w);
-    sh->ctx.t_end = c.split.begin(c.w + 1);
-    sh->ctx.tmem = sh->tmem_base;
-  }
-  __syncthreads();
-  const Ctx& cs = sh->ctx;
-
+  const bool hit = __syncthreads_and(same);
   if (warp == kKWarp) {
+    // Warp 0 builds the plan and the launch context alone, releases the other
+    // warps, and goes on as the K producer.  The roles read the context from
+    // shared memory (one copy per CTA) rather than from a stack copy per
+    // thread, which would live in local memory.
+    Ctx c;
+    c.p = &p;
+    c.sh = sh;
+    c.smem = smem;
+    c.ps = PlanSmem{plan_mem, plan_mem + (p.num_rows + 1), plan_mem + 2 * (p.num_rows + 1),
+                    plan_mem + 2 * (p.num_rows + 1) + 8};
+    if (!hit) build_plan_warp(c.ps, p.seq_ids, p.seq_lens, p.num_rows, p.max_group_rows);
+    c.ng = c.ps.misc[0];
+    c.hk = p.num_kv_heads;
+    c.gqa = p.num_q_heads / p.num_kv_heads;
+    c.oob_row = args.oob_row;
+    c.total = (long long)c.hk * c.ps.gprefix[c.ng];
+    const long long launched = gridDim.x;
+    c.w = blockIdx.x;
+    c.split.gprefix = c.ps.gprefix;
+    c.split.ng = c.ng;
+    c.split.hk = c.hk;
+    c.split.pc = kPieceCost;
+    c.split.vtotal = c.total + (long long)kPieceCost * c.hk * c.ng;
+    c.workers = c.total == 0 ? 0 : (launched < c.split.vtotal ? launched : c.split.vtotal);
+    c.split.workers = c.workers;
+    if (hit) {
+      c.t_begin = sh->cached_begin;
+      c.t_end = sh->cached_end;
+      c.g_begin = sh->cached_group;
+    } else {
+      long long edge = 0;  // lanes 0 and 1: the first tiles of workers w and w + 1
+      if (c.w < c.workers && lane < 2) edge = c.split.begin(c.w + lane);
+      c.t_begin = __shfl_sync(0xffffffffu, edge, 0);
+      c.t_end = __shfl_sync(0xffffffffu, edge, 1);
+      c.g_begin = c.t_begin < c.t_end ? find_group(c.ps.gprefix, c.ng, c.t_begin, c.hk) : 0;
+    }
+    c.pc_hit = hit;
+    c.seq = args.seq;
+    c.pc_entry = cacheable ? p.plan_cache + (args.seq & 1u) * kPcSlotWords + kPcWorkers + blockIdx.x * kPcEntryWords
+                           : nullptr;
+    c.tmem = sh->tmem_base;
+    if (lane == 0) sh->ctx = c;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sh->plan_ready);
+  }
+  const bool planned = warp == kKWarp || wait_or_abort(sh, p, &sh->plan_ready, 0);
+  const Ctx& cs = sh->ctx;
+  // The epilogue warps, idle until the first piece ends, leave this call's
+  // plan for the next call: every CTA its own range, CTA 0 the rest.
+  if (planned && cacheable && warp >= kEpiWarp0) {
+    const int t = threadIdx.x - kEpiWarp0 * 32;
+    int32_t* wr = p.plan_cache + (args.seq & 1u) * kPcSlotWords;
+    if (cs.w >= cs.workers && t == 0) {  // a CTA without tiles (the K warp writes the others' entries)
+      int32_t* wk = wr + kPcWorkers + blockIdx.x * kPcEntryWords;
+      *reinterpret_cast<long long*>(wk + 2) = cs.t_begin;
+      *reinterpret_cast<long long*>(wk + 4) = cs.t_end;
+      wk[1] = cs.g_begin;
+      wk[0] = (int32_t)args.seq;
+    }
+    if (blockIdx.x == 0) {
+      for (int i = t; i < p.num_rows; i += kEpiThreads) {
+        wr[kPcIds + i] = __ldcg(p.seq_ids + i);
+        wr[kPcLens + i] = __ldcg(p.seq_lens + i);
+      }
+      for (int i = t; i < 3 * (p.num_rows + 1) + 8; i += kEpiThreads) wr[kPcPlan + i] = plan_mem[i];
+      if (t == 0) {
+        wr[0] = (int32_t)kPlanCacheMagic;
+        wr[1] = (int32_t)args.seq;
+        wr[2] = p.num_rows;
+        wr[3] = p.max_group_rows;
+        wr[4] = p.num_kv_heads;
+        wr[5] = p.num_q_heads;
+        wr[6] = (int)gridDim.x;
+        wr[7] = kPieceCost;
+        wr[8] = p.mbs;
+        wr[9] = p.bt_rows;
+      }
+    }
+  }
+  if (planned && warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4)
+    write_nan_rows(p, cs.ps, cs.ng, cs.w * 4 + (warp - kSoftmaxWarp0), (long long)gridDim.x * 4);
+  const bool work = planned && cs.w < cs.workers;  // uniform over the CTA unless the wait gave up
+  if (!work) {
+  } else if (warp == kKWarp) {
     FirstSplit first;
     first.pending = false;
     producer(cs, &tmap_k, sh->k_full, sh->k_empty, kKOff, kKRing, 1, &first);
@@ -1210,8 +1332,8 @@ __global__ void __launch_bounds__(kVThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == kSWarp) tmem_dealloc(cs.tmem, kTmemCols);
-  if (!aborted(sh) && (sh->first_last || sh->last_merge)) finish_units(cs);
+  if (warp == kSWarp) tmem_dealloc(sh->tmem_base, kTmemCols);
+  if (work && !aborted(sh) && (sh->first_last || sh->last_merge)) finish_units(cs);
 }
 
 // ------------------------------------------------------------------ host side
@@ -1328,6 +1450,14 @@ int launch_verify(const AttnParams& p, long long workers, cudaStream_t stream) {
   VerifyArgs a;
   a.p = p;
   a.oob_row = (int)rows;
+  {
+    // Launch number per workspace: calls on one workspace are ordered on one
+    // stream, so call n may use the plan left by call n - 1.
+    static std::mutex seq_mu;
+    static std::unordered_map<const void*, uint32_t> seq_of;
+    std::lock_guard<std::mutex> lock(seq_mu);
+    a.seq = ++seq_of[p.hdr];
+  }
   const size_t smem = verify_smem_bytes(p.num_rows);
   int device = 0;
   NEB_CUDA(cudaGetDevice(&device));

@@ -268,3 +268,24 @@ def test_counters_return_to_zero_across_shapes(kernel, cuda):
         out = run_attention(c, kernel, cuda, workspace=ws)
         assert int(torch.count_nonzero(counters).item()) == 0, f"stale counters after {shape}"
         torch.testing.assert_close(out, oracle_of(c), atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("kernel", ["verify"] if VERIFY_BUILT else [])
+def test_plan_cache_follows_inputs(kernel, cuda):
+    """The verify kernel reuses the previous call's work plan on the same
+    workspace only when the rows' seq ids, lengths and the call's shape are the
+    same: repeated, changed and restored batches on one workspace all match the
+    oracle, as do calls after the block table's contents or width change."""
+    from nebulasd_b200._workspace import attention_workspace
+    stream = torch.cuda.current_stream(cuda)
+    ws = attention_workspace(_kernel_id(kernel), cuda, stream, 512, 32, 8)
+    a = batch_case(71, **SHAPES["verify_gqa4_k4"])
+    b = batch_case(72, **SHAPES["verify_gqa4_k4"])          # same shapes, other lengths
+    c = dict(a, seq_ids=a["seq_ids"].flip(0).contiguous(), seq_lens=a["seq_lens"].flip(0).contiguous(),
+             q=a["q"].flip(0).contiguous())  # rows reordered
+    moved = dict(a, block_table=a["block_table"].roll(1, dims=0).contiguous(),
+                 seq_ids=((a["seq_ids"] + 1) % a["block_table"].shape[0]).to(torch.int32))  # same blocks, other rows
+    wide = dict(a, block_table=torch.cat([a["block_table"], torch.full_like(a["block_table"], -1)], 1))
+    for case in (a, a, b, a, a, c, a, moved, moved, wide, wide, a):
+        torch.testing.assert_close(run_attention(case, kernel, cuda, workspace=ws), oracle_of(case),
+                                   atol=ATOL, rtol=RTOL)
