@@ -154,7 +154,6 @@ struct VerifyShared {
   uint64_t st_full[2];           // the softmax wrote piece i's row statistics (one arrival per warp)
   uint64_t st_empty[2];          // the epilogue read them
   uint64_t plan_ready;           // warp 0 wrote the plan and the context
-  uint64_t part_ready;           // softmax wrote the partial of the CTA's first piece (split, not last)
   uint64_t s_final;
   uint64_t pv_final;
   uint32_t tmem_base;
@@ -384,38 +383,20 @@ struct TileFeed {
   }
 };
 
-// The first piece of a worker's range, when it is part of a unit split across
-// CTAs and not the worker's only piece: the K warp counts its partial in as
-// soon as the softmax has written it, so that the CTA finishing the unit's
-// other part (late, as its last piece) finds it in and merges directly.
+// The first piece of a worker's range (a unit split across CTAs): its group,
+// kv head and the unit's first and last workers, for the merge at the end
+// when counting this piece in completed the unit.
 struct FirstSplit {
-  bool pending;
-  long long unit, w0, w1;
+  long long w0, w1;
   int g, h;
   __device__ __noinline__ void init(const Ctx& c) {
     PieceCursor cur;
     cur.init(&c.ps, c.ng, c.hk, c.t_begin, c.t_end, c.g_begin);
     int lo, hi, nb;
     long long ustart;
-    pending = false;
-    if (!cur.next(g, h, lo, hi, nb, ustart)) return;
-    if ((lo == 0 && hi == nb) || c.t_begin + (hi - lo) >= c.t_end) return;
-    pending = true;
-    unit = (long long)g * c.hk + h;
+    cur.next(g, h, lo, hi, nb, ustart);
     w0 = c.split.worker_of_tile(ustart);
     w1 = c.split.worker_of_tile(ustart + nb - 1);
-  }
-  // Lane-0 work once the softmax has arrived: publish the partial and count it.
-  __device__ __noinline__ void count(const Ctx& c) {
-    // The mbarrier wait ordered the softmax warps' partial stores before this
-    // fence, which publishes them with the count.
-    __threadfence();
-    const int last = atomicAdd(c.p->counters + unit, 1) == (int)(w1 - w0);
-    if (last) {
-      c.p->counters[unit] = 0;  // every piece has arrived: ready for the next call
-      c.sh->first_last = 1;
-    }
-    pending = false;
   }
 };
 
@@ -432,7 +413,7 @@ struct FirstSplit {
 // flags before it releases its S: flag slots with kFlagSlots >= kKRing +
 // kSBufs are free.
 __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uint64_t* full, uint64_t* empty,
-                                      uint32_t ring_off, int ring, int flags, FirstSplit* first) {
+                                      uint32_t ring_off, int ring, int flags) {
   const AttnParams& p = *c.p;
   VerifyShared* sh = c.sh;
   const int lane = threadIdx.x & 31;
@@ -487,21 +468,17 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
       }
     }
     // Once the first loads are on their way, the K warp leaves its range for
-    // the next call and works out which piece (if any) it counts in early.
-    if (first && G == 0) {
-      if (c.pc_entry) {
+    // the next call.
+    if (flags && G == 0 && c.pc_entry) {
 #pragma unroll
-        for (int k = 0; k < 3; ++k) reinterpret_cast<long long*>(c.pc_entry + kPcEntryFeed)[32 * k + lane] = e[k];
-        if (lane == 0) {
-          c.pc_entry[1] = c.g_begin;
-          *reinterpret_cast<long long*>(c.pc_entry + 2) = c.t_begin;
-          *reinterpret_cast<long long*>(c.pc_entry + 4) = c.t_end;
-          c.pc_entry[0] = (int32_t)c.seq;
-        }
+      for (int k = 0; k < 3; ++k) reinterpret_cast<long long*>(c.pc_entry + kPcEntryFeed)[32 * k + lane] = e[k];
+      if (lane == 0) {
+        c.pc_entry[1] = c.g_begin;
+        *reinterpret_cast<long long*>(c.pc_entry + 2) = c.t_begin;
+        *reinterpret_cast<long long*>(c.pc_entry + 4) = c.t_end;
+        c.pc_entry[0] = (int32_t)c.seq;
       }
-      first->init(c);
     }
-    if (lane == 0 && first && first->pending && mbar_test_wait(&sh->part_ready, 0)) first->count(c);
     if (!waited) break;
     ++used;
     pos += n0;
@@ -513,7 +490,6 @@ __device__ __noinline__ void producer(const Ctx& c, const CUtensorMap* tmap, uin
     }
     more = next_stage(n0);
   }
-  if (lane == 0 && first && first->pending && wait_or_abort(sh, p, &sh->part_ready, 0)) first->count(c);
   // Wait (bounded) for every copy this warp issued before the CTA can exit.
   if (lane == 0)
 #pragma unroll 1
@@ -716,11 +692,11 @@ struct SoftmaxRows {
 // go on with the next piece): O / l as fp16 output rows, or, for a unit split
 // across CTAs, a partial (O / l and m + log2 l).  m and l are the rows' final
 // max and sum.  The last piece of the CTA's range first looks at the unit's
-// counter: when the one other piece has been counted in already, it merges
-// that partial with its own O directly.  Otherwise it writes its partial and
-// counts it in, and if that completes the unit the epilogue warps merge the
-// partials.  The first piece's partial is counted in by the K warp.  The PV
-// issuer may reuse the piece's O buffer once it has been read.
+// counter: when the other pieces have been counted in already, it merges
+// their partials with its own O directly.  Otherwise it writes its partial
+// and counts it in; the count that completes a unit leaves the merge of its
+// partials to the whole CTA at the end (finish_units).  The PV issuer may
+// reuse the piece's O buffer once it has been read.
 __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, int piece, float m_a, float m_b,
                                             float l_a, float l_b, bool last_piece) {
   const AttnParams& p = *c.p;
@@ -838,20 +814,24 @@ __device__ __noinline__ bool piece_epilogue(const Ctx& c, const SoftmaxRows& r, 
   if (!whole) {
     if (direct) {
       if (tid == 0) p.counters[unit] = 0;  // the unit is complete: ready for the next call
-    } else if (!last_piece) {
-      warp_arrive(&sh->part_ready);  // the K warp counts it in
     } else {
+      // Count the partial in (the first piece of a range, or the last); the
+      // count that completes the unit leaves its merge to the whole CTA once
+      // every role is done.
       named_bar_sync(2, kEpiThreads);  // every partial store precedes thread 0's fence
       if (tid == 0) {
         __threadfence();
-        // Completing the unit: the whole CTA merges it once every role is done.
         if (atomicAdd(p.counters + unit, 1) == (int)(w1 - w0)) {
-          p.counters[unit] = 0;
-          sh->lm_g = r.g;
-          sh->lm_h = r.h;
-          sh->lm_w0 = w0;
-          sh->lm_w1 = w1;
-          sh->last_merge = 1;
+          p.counters[unit] = 0;  // every piece has arrived: ready for the next call
+          if (!last_piece) {
+            sh->first_last = 1;
+          } else {
+            sh->lm_g = r.g;
+            sh->lm_h = r.h;
+            sh->lm_w0 = w0;
+            sh->lm_w1 = w1;
+            sh->last_merge = 1;
+          }
         }
       }
     }
@@ -1161,7 +1141,6 @@ __global__ void __launch_bounds__(kVThreads, 1)
       mbar_init(&sh->st_empty[i], 4);
     }
     mbar_init(&sh->plan_ready, 1);
-    mbar_init(&sh->part_ready, 4);
     sh->first_last = 0;
     sh->last_merge = 0;
     mbar_init(&sh->s_final, 1);
@@ -1315,11 +1294,9 @@ __global__ void __launch_bounds__(kVThreads, 1)
   const bool work = planned && cs.w < cs.workers;  // uniform over the CTA unless the wait gave up
   if (!work) {
   } else if (warp == kKWarp) {
-    FirstSplit first;
-    first.pending = false;
-    producer(cs, &tmap_k, sh->k_full, sh->k_empty, kKOff, kKRing, 1, &first);
+    producer(cs, &tmap_k, sh->k_full, sh->k_empty, kKOff, kKRing, 1);
   } else if (warp == kVWarp) {
-    producer(cs, &tmap_v, sh->v_full, sh->v_empty, kVOff, kVRing, 0, nullptr);
+    producer(cs, &tmap_v, sh->v_full, sh->v_empty, kVOff, kVRing, 0);
   } else if (warp == kSWarp) {
     if (lane == 0) s_issuer(cs, &tmap_q);
   } else if (warp == kPVWarp) {
