@@ -69,6 +69,8 @@ def _args():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--layers", type=int, default=None,
                     help="override the workload's layer count (profiling: a small pool, same per-call shape)")
+    ap.add_argument("--requests", type=int, default=None,
+                    help="override the workload's request count (profiling: a smaller pool, same per-request shape)")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s clock-sampling soak (profiling runs)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the secondary figures (reference kernels on this GPU, configs 2, 2b and 4)")
@@ -165,12 +167,15 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_workload(name: str, seed: int, device, layers_override=None):
+def build_workload(name: str, seed: int, device, layers_override=None, requests_override=None):
     from nebulasd_b200.workloads import CONFIGS, make_paged_batch
     cfg = dict(CONFIGS[name])
     layers = cfg.pop("num_layers", 1)
     if layers_override:
         layers = layers_override
+    if requests_override:  # profiling: fewer requests, a pool scaled to match
+        cfg["pool_blocks"] = -(-cfg["pool_blocks"] * requests_override // cfg["num_requests"])
+        cfg["num_requests"] = requests_override
     b = make_paged_batch(seed, num_layers=layers, cur_layer=0, device=device, **cfg)
     return b, layers, cfg
 
@@ -195,7 +200,7 @@ def run_ours(args):
     from nebulasd_b200.kernels.paged_attn import choose_kernel, set_kernel
     set_kernel(args.kernel)
 
-    b, layers, cfg = build_workload(args.workload, 1234 + 7919 * rank, dev, args.layers)
+    b, layers, cfg = build_workload(args.workload, 1234 + 7919 * rank, dev, args.layers, args.requests)
     kernel = choose_kernel(b.num_q_heads, b.num_kv_heads, int(b.q.shape[0]), max(b.seq_lens_list))
     kname = {_lib.NEB_ATTN_DECODE: "decode", _lib.NEB_ATTN_VERIFY: "verify",
              _lib.NEB_ATTN_VERIFY_LONG: "verify_long"}[kernel]
@@ -493,12 +498,13 @@ def secondary_attention(workload, dev, steps):
                       _lib.NEB_ATTN_VERIFY_LONG: "verify_long"}[kernel],
            "requests": cfg["num_requests"], "depth": cfg["depth"], "ctx": [cfg["ctx_lo"], cfg["ctx_hi"]],
            "num_layers": layers}
+    out["traffic_profile"] = _traffic(workload, out["kernel"])
     k_cache_free(b)
     torch.cuda.empty_cache()
     return out
 
 
-def fused_bar(dev):
+def fused_bar(dev, layers_override=None):
     """Config 2b: QK-RMSNorm + RoPE + KV store of the Draft's 64 decode tokens
     (Qwen3-0.6B: 16 q / 8 kv heads, 28-layer pool), our single launch against
     the reference's four Triton launches (``transformer_layer.py:114-143``) on
@@ -508,6 +514,8 @@ def fused_bar(dev):
     from baseline import reference as R
     cfg = dict(CONFIGS["draft_decode_0p6b"])
     layers = cfg.pop("num_layers")
+    if layers_override:  # profiling: a smaller pool, same per-call work
+        layers = layers_override
     cfg["pool_blocks"] = 8192  # holds the batch's blocks; smaller than config 2's pool, so the set-up is short
     b = make_paged_batch(77, num_layers=layers, cur_layer=0, device=dev, **cfg)
     T, H, D = b.q.shape
@@ -780,9 +788,30 @@ def run_migrate(args):
     }), flush=True)
 
 
+def run_fused(args):
+    """Config 2b on its own line: the fused QK-RMSNorm + RoPE + KV store of the
+    Draft's 64 decode tokens, one launch, against the reference's four Triton
+    launches on the same inputs (rank 0 only)."""
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    r = fused_bar(torch.device("cuda", local), args.layers)
+    line = {"metric": "fused QK-RMSNorm + RoPE + KV-store us per call (Qwen3-0.6B, 64 decode tokens)",
+            "value": r["ours_us"], "unit": "us", "n_gpus": 1, "higher_is_better": False, "scaling": "none",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "fused_store_0p6b", "tokens": r["tokens"], "launches": r["ours_launches"],
+                       "num_layers": args.layers or 28,
+                       "bytes_per_call": r["bytes"]},
+            "reference_gpu": {k: r[k] for k in ("reference_launches", "reference_us", "ours_speedup") if k in r}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
-    if args.workload == "hostkv_copy":
+    if args.workload == "fused_store_0p6b":
+        run_fused(args)
+    elif args.workload == "hostkv_copy":
         run_hostkv(args)
     elif args.workload == "kv_migrate":
         run_migrate(args)
