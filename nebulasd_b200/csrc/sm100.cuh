@@ -111,6 +111,17 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* tmap, ui
       : "memory");
 }
 
+// Prefetch of one 2D box into L2 (a hint: no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)
+               : "memory");
+}
+
+// Prefetch of the 128-byte line holding `p` into L2 (a hint).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // 3D tiled load of one box into shared memory, completing on `bar` (no multicast).
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int x, int y, int z) {
   asm volatile(

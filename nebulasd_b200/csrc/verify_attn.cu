@@ -1160,6 +1160,36 @@ __global__ void __launch_bounds__(kVThreads, 1)
   tc_fence_before();
   __syncthreads();  // barriers and the tensor-memory address are visible to every thread
   tc_fence_after();
+  if (warp == kEpiWarp0 && gridDim.x <= kPlanCacheWorkers && p.num_rows <= kMaxRows) {
+    // While the previous launch finishes, an idle warp brings into L2 what the
+    // call will read first, as the previous call on this workspace left it:
+    // the plan cache slot and rows it checks, and the first two stages of this
+    // worker's K and V.  Prefetches are hints: if the previous call's plan is
+    // not this call's (or is being written), they only waste bandwidth; every
+    // value used is read again after the wait.
+    const int32_t* rd = p.plan_cache + (((args.seq & 1u) ^ 1u) * kPcSlotWords);
+    const int32_t* wk = rd + kPcWorkers + blockIdx.x * kPcEntryWords;
+    const long long e = __ldcg(reinterpret_cast<const long long*>(wk + kPcEntryFeed) + lane);
+    for (int i = lane * 32; i < p.num_rows; i += 32 * 32) {
+      prefetch_l2(p.seq_ids + i);
+      prefetch_l2(p.seq_lens + i);
+      prefetch_l2(rd + kPcIds + i);
+      prefetch_l2(rd + kPcLens + i);
+    }
+    for (int i = lane * 32; i < 3 * (p.num_rows + 1) + 8; i += 32 * 32) prefetch_l2(rd + kPcPlan + i);
+    if (lane == 0) prefetch_l2(rd);
+    if (lane < 2 * kStageBlocks && e >= 0 && (e >> 8) < (long long)p.bt_rows * p.mbs &&
+        (int)(e & 255) < p.num_kv_heads) {
+      const long long blk = __ldcg(p.block_table + (e >> 8));
+      if (blk >= 0 && blk < p.num_blocks) {
+        const int row = (int)(((blk * p.num_layers + p.cur_layer) * p.num_kv_heads + (int)(e & 255)) * kBlockTokens);
+        tma_prefetch_2d(&tmap_k, 0, row);
+        tma_prefetch_2d(&tmap_k, 64, row);
+        tma_prefetch_2d(&tmap_v, 0, row);
+        tma_prefetch_2d(&tmap_v, 64, row);
+      }
+    }
+  }
   grid_dependency_wait();  // inputs may come from the previous launch in the stream
   // The plan of the previous call on this workspace, if it is this call's:
   // every thread loads a share of it and of the rows' seq ids and lengths in
