@@ -437,6 +437,23 @@ def _time_steps(fn, steps, warmup=2):
     return e0.elapsed_time(e1) / steps
 
 
+def _time_queued(fn, steps, warmup=3):
+    """Device time per call of a launch-bound op: the stream is held behind a
+    GPU sleep while the calls are queued, so host launch overhead cannot
+    leave the GPU idle between them."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(int(2e8))  # about 0.1 s at the B200's clock: room to queue every call
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
 def reference_gpu_bar(b, layers, scale, our_launch_ms):
     """The reference's own Triton ``paged_attention`` (phase 1 + phase 2,
     ``swiftLLM/swiftllm/worker/kernels/paged_attn.py:152-222``), JIT-compiled by
@@ -807,9 +824,96 @@ def run_fused(args):
     print(json.dumps(line), flush=True)
 
 
+def run_accept(args):
+    """Greedy acceptance of a Qwen3-8B verify batch (16 requests x (k+1 = 5)
+    rows x 151,936 fp16 logits, 24.3 MB): the device kernel (arg-max and
+    acceptance, results left on the GPU) against the reference's tail on the
+    same GPU: ``torch.argmax``, ``.tolist()`` and ``compute_greedy_acceptance``
+    per request (``post_layer.py:72``, ``model.py:465``, ``speculative.py:122-156``)."""
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from nebulasd_b200.accept import greedy_accept
+    from baseline import reference as R
+    reqs, depth, vocab = 16, 4, 151936
+    rows = reqs * (depth + 1)
+    g = torch.Generator(device=dev).manual_seed(99)
+    logits = (torch.randn((rows, vocab), generator=g, device=dev) * 4).half()
+    am = logits.argmax(1).view(reqs, depth + 1)
+    drafts = am[:, :depth].clone()
+    drafts[::2, 2] += 1  # half the requests stop accepting at their third draft
+    row_start = torch.arange(0, rows + 1, depth + 1, dtype=torch.int32, device=dev)
+    flat = drafts.to(torch.int32).reshape(-1).contiguous()
+
+    from nebulasd_b200 import _lib
+    from nebulasd_b200.accept import _workspace
+    result = torch.empty(reqs * (depth + 1) + 2 * reqs + rows, dtype=torch.int32, device=dev)  # one readback
+    tokens = result[:reqs * (depth + 1)].view(reqs, depth + 1)
+    count = result[reqs * (depth + 1):reqs * (depth + 2)]
+    accepted = result[reqs * (depth + 2):reqs * (depth + 3)]
+    amax = result[reqs * (depth + 3):]
+    stream = torch.cuda.current_stream(dev)
+    ws = _workspace(dev, stream, rows)
+    args_c = (logits.data_ptr(), vocab, vocab, rows, row_start.data_ptr(), reqs, flat.data_ptr(), None, None, 0,
+              depth + 1, amax.data_ptr(), tokens.data_ptr(), count.data_ptr(), accepted.data_ptr(), ws.data_ptr(),
+              ws.numel(), stream.cuda_stream)
+
+    def kernel_only():  # the C ABI with resident buffers: device time of the kernel
+        _lib.lib.neb_greedy_accept(*args_c)
+
+    def api():  # the Python API, results read back as the reference's tuples need them
+        greedy_accept(logits, row_start, flat, out=(tokens, count, accepted, amax))
+        return result.cpu()
+
+    steps = max(args.steps, 50)
+    us = _time_queued(kernel_only, steps, max(args.warmup, 3)) * 1e3
+    for _ in range(3):
+        api()
+    t0 = time.perf_counter()
+    for _ in range(20):
+        api()
+    api_us = (time.perf_counter() - t0) / 20 * 1e6
+    moved = rows * vocab * 2
+    peak, peak_kind = _peaks()
+    achieved = moved / (us * 1e-6) / 1e9
+    line = {"metric": "greedy accept us per verify batch (Qwen3-8B: 16 requests x 5 rows x 151,936 logits)",
+            "value": round(us, 2), "unit": "us", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 3),
+            "higher_is_better": False, "scaling": "none", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "greedy_accept_8b", "requests": reqs, "depth": depth, "vocab": vocab,
+                       "l2": "the 24.3 MB of logits fit L2, as they do after the lm_head GEMM that writes them"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "bytes_per_call": moved},
+            "gpu_launches": steps,
+            "e2e": {"value": round(api_us, 2), "unit": "us", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": result.numel() * 4,
+                    "api": "nebulasd_b200.accept.greedy_accept + copy of the results to the host"}}
+    if R.available():
+        spec = R.swiftllm("speculative")
+        dl = drafts.tolist()
+
+        def ref():
+            post = torch.argmax(logits, dim=1).tolist()
+            return [spec.compute_greedy_acceptance(dl[r], post[r * (depth + 1):(r + 1) * (depth + 1)])
+                    for r in range(reqs)]
+
+        for _ in range(3):
+            ref()
+        t0 = time.perf_counter()
+        for _ in range(20):
+            ref()
+        ref_us = (time.perf_counter() - t0) / 20 * 1e6
+        line["reference_gpu"] = {"impl": "torch.argmax + .tolist() + compute_greedy_acceptance (host), same logits",
+                                 "us": round(ref_us, 2), "host_sync": True}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
-    if args.workload == "fused_store_0p6b":
+    if args.workload == "greedy_accept_8b":
+        run_accept(args)
+    elif args.workload == "fused_store_0p6b":
         run_fused(args)
     elif args.workload == "hostkv_copy":
         run_hostkv(args)

@@ -161,6 +161,37 @@ int neb_paged_attention_verify_long(const void* q, const void* k_cache, const vo
  * so call it before reusing a workspace whose last call may have failed. */
 int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream);
 
+/* ---------------------------------------------------------------- greedy accept
+ * Greedy speculative acceptance on the device.  Replaces the verify-side tail
+ * of the reference: torch.argmax of the logits
+ * (swiftLLM/swiftllm/worker/layers/post_layer.py:72), the .tolist() of the
+ * posterior tokens (swiftLLM/swiftllm/worker/model.py:465) and
+ * compute_greedy_acceptance (swiftLLM/swiftllm/speculative.py:122-156), with
+ * no host synchronisation.  No reference function takes these arguments; the
+ * Python face is nebulasd_b200.accept.greedy_accept.
+ *
+ * logits        fp16 [num_rows][row_stride], the first `vocab` of each row used
+ * row_start     [num_requests + 1]: request r owns rows row_start[r] ..
+ *               row_start[r+1]-1 (k + 1 rows for k draft tokens)
+ * draft_tokens  [num_rows - num_requests]: request r's k drafts start at
+ *               row_start[r] - r
+ * remaining     [num_requests] output budget (-1: none) or NULL
+ * stop_tokens   [num_stop]
+ * out_tokens    [num_requests][max_out]: the tokens to append, then -1
+ * out_count     [num_requests]: how many; out_accepted: accepted drafts
+ * argmax_out    [num_rows] arg-max per row (ties: lowest index; NaN counts as
+ *               the largest value), or NULL
+ * All arrays are device memory.  The workspace
+ * (neb_greedy_accept_workspace_bytes) is zero-filled once and left zero by
+ * every call; calls sharing it must be ordered on one stream.  Invalid rows or
+ * budgets are recorded as error bit 4 (read with neb_workspace_status). */
+size_t neb_greedy_accept_workspace_bytes(int32_t num_rows);
+int neb_greedy_accept(const void* logits, int64_t row_stride, int32_t vocab, int32_t num_rows,
+                      const int32_t* row_start, int32_t num_requests, const int32_t* draft_tokens,
+                      const int32_t* remaining, const int32_t* stop_tokens, int32_t num_stop, int32_t max_out,
+                      int32_t* argmax_out, int32_t* out_tokens, int32_t* out_count, int32_t* out_accepted,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------ QK-norm, RoPE and KV store
  * Token layout of one forward (the reference's): prefill tokens first
  * (sequence s occupies [prefill_start_locs[s], +prefill_seq_lens[s]) with

@@ -45,6 +45,9 @@ SIGNATURES = {
     "neb_kv_peer_copy": ([_vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _vp], ctypes.c_int),
     "neb_host_device_pointer": ([_vp, ctypes.POINTER(_vp)], ctypes.c_int),
     "neb_enable_peer_access": ([ctypes.c_int], ctypes.c_int),
+    "neb_greedy_accept_workspace_bytes": ([_i32], _sz),
+    "neb_greedy_accept": ([_vp, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
+                           _sz, _vp], ctypes.c_int),
 }
 
 for _name, (_args, _res) in SIGNATURES.items():

@@ -41,7 +41,10 @@ enum DeviceError : uint32_t {
   kErrSeqId = 1u << 1,        // seq_id outside [0, block_table_rows)
   kErrTooManyBlocks = 1u << 2,  // sequence needs more than max_blocks_per_seq blocks
   kErrTimeout = 1u << 3,      // a bounded wait gave up
+  kErrInvalidRows = 1u << 4,  // greedy accept: a request's rows or output limit are invalid
 };
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Workspace header shared by the attention kernels (first 256 bytes).
 struct WorkspaceHeader {

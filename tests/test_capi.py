@@ -18,6 +18,7 @@ def test_header_declares_the_hot_path():
     names = declared_symbols()
     for must in ("neb_paged_attention_decode", "neb_paged_attention_verify", "neb_store_kvcache",
                  "neb_qk_norm_rope_store", "neb_rotary_inplace", "neb_rmsnorm_inplace", "neb_hostkv_copy",
+                 "neb_greedy_accept", "neb_greedy_accept_workspace_bytes",
                  "neb_kv_peer_copy"):
         assert must in names
 
@@ -107,3 +108,32 @@ def test_copy_mode_choice_by_run_length():
     assert choose_copy_mode(short, block, mapped=True) == "memcpy"  # 1.18 MB per run is long enough
     assert choose_copy_mode(short, 4096, mapped=False) == "memcpy"  # unmapped arena: engines only
     assert choose_copy_mode(np.zeros((0, 3), dtype=np.int64), block, mapped=True) == "kernel"
+
+
+def test_greedy_accept_rejects_bad_arguments_on_the_host():
+    """Argument checks run before any device work (no GPU needed)."""
+    from nebulasd_b200 import _lib
+    lib = _lib.lib
+    assert lib.neb_greedy_accept_workspace_bytes(80) >= 256 + 80 * 8
+    args = [16, 1000, 100, 4, 16, 2, 16, None, None, 0, 5, None, 16, 16, 16, 256, 4096, None]
+    bad = list(args); bad[2] = 0                  # empty vocabulary
+    assert lib.neb_greedy_accept(*bad) != 0
+    bad = list(args); bad[1] = 10                 # row stride shorter than the vocabulary
+    assert lib.neb_greedy_accept(*bad) != 0
+    bad = list(args); bad[5] = 5                  # more requests than rows
+    assert lib.neb_greedy_accept(*bad) != 0
+    ok_empty = list(args); ok_empty[3] = 0; ok_empty[5] = 0
+    assert lib.neb_greedy_accept(*ok_empty) == 0  # nothing to do
+    bad = list(args); bad[16] = 8                 # workspace too small
+    assert lib.neb_greedy_accept(*bad) != 0
+
+
+def test_accept_batch_validates_like_the_reference():
+    import pytest as _pytest
+    import torch
+    from nebulasd_b200.accept import compute_greedy_acceptance_batch
+    logits = torch.zeros((5, 10), dtype=torch.float16)
+    with _pytest.raises(ValueError, match="K\\+1"):
+        compute_greedy_acceptance_batch([[1, 2, 3, 4, 5]], logits)
+    with _pytest.raises(ValueError, match="non-negative"):
+        compute_greedy_acceptance_batch([[1, 2, 3, 4]], logits, remaining_output_len=[-1])
