@@ -909,9 +909,164 @@ def run_accept(args):
     print(json.dumps(line), flush=True)
 
 
+def run_long_hostkv(args):
+    """Config 4 with its HostKV traffic (rank 0): 64 requests, ctx U[8K, 32K];
+    bank B (a quarter of the requests) restores its full KV from the pinned
+    host arena through NativeCopyBackend while bank A (the rest) runs
+    long-context verify, and every verify round writes bank A's changed blocks
+    (the k+1 new tokens) back on a second backend stream (``fork``).  The arena,
+    extents and plans are the reference's (``SharedHostKVArena``, ``CopyPlan``)."""
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    import numpy as np
+    from baseline import reference as R
+    from nebulasd_b200.hostkv import NativeCopyBackend
+    from nebulasd_b200.kernels import paged_attention_raw
+    workload = args.workload.replace("_hostkv", "")
+    metric = f"long-context verify TB/s with HostKV restore overlapped ({workload})"
+    if not R.available():
+        print(json.dumps({"metric": metric, "unavailable": "reference not installed under baseline/_ref"}), flush=True)
+        return
+    arena_mod, tr = R.nebulasd("kv.arena"), R.nebulasd("kv.transfer")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    b, layers, cfg = build_workload(workload, 1234, dev, None, args.requests)
+    nreq = cfg["num_requests"]
+    nb_restore = nreq // 4
+    bt = b.block_table.cpu().numpy()
+    depths = list(b.depths)
+    ctx = list(b.ctx)
+    row_first = np.cumsum([0] + [d + 1 for d in depths])
+    # Bank A: requests nb_restore.. (their rows are the tail of the batch).
+    ra = int(row_first[nb_restore])
+    qa, lens_a, ids_a = b.q[ra:].contiguous(), b.seq_lens[ra:].contiguous(), b.seq_ids[ra:].contiguous()
+    oa = torch.empty_like(qa)
+    scale = b.q.shape[-1] ** -0.5
+    a_bytes = int(sum(-(-(c + d + 1) // 16) for c, d in zip(ctx[nb_restore:], depths[nb_restore:]))) \
+        * b.num_kv_heads * 16 * 128 * 2 * 2
+    block_bytes = b.k_cache[0].numel() * 2
+    kv_shape = tuple(b.k_cache.shape[1:])
+    restore_blocks = [-(-ctx[i] // 16) for i in range(nb_restore)]
+    wb_blocks = 2
+    total_host = sum(restore_blocks) + wb_blocks * (nreq - nb_restore)
+    try:
+        arena = arena_mod.SharedHostKVArena.create(total_blocks=total_host, block_bytes=block_bytes,
+                                                   dtype=str(b.k_cache.dtype), kv_block_shape=kv_shape)
+    except OSError as e:
+        print(json.dumps({"metric": metric, "unavailable": f"shared-memory arena: {e}"}), flush=True)
+        return
+    host = np.ctypeslib.as_array((__import__("ctypes").c_uint8 * arena.descriptor.total_bytes)
+                                 .from_address(arena.address()))
+    host[:] = np.random.default_rng(7).integers(0, 256, host.shape[0], dtype=np.uint8)
+    regions, off = [], 0
+    for i in range(nb_restore):
+        ext = arena.make_extent(request_slot=i, request_epoch=1, host_slot=i, host_slot_generation=1,
+                                writer_lease_generation=1, offset_blocks=off, capacity_blocks=restore_blocks[i])
+        j = 0
+        while j < restore_blocks[i]:  # one region per run of consecutive GPU blocks
+            n = 1
+            while j + n < restore_blocks[i] and bt[i, j + n] == bt[i, j] + n:
+                n += 1
+            regions.append(tr.CopyRegion(ext, int(bt[i, j]), j, n))
+            j += n
+        off += restore_blocks[i]
+    restore_plan = tr.CopyPlan("H2D", tuple(regions))
+    wb_regions = []
+    for k, i in enumerate(range(nb_restore, nreq)):
+        ext = arena.make_extent(request_slot=nb_restore + k, request_epoch=1, host_slot=nb_restore + k,
+                                host_slot_generation=1, writer_lease_generation=1, offset_blocks=off,
+                                capacity_blocks=wb_blocks)
+        first, last = ctx[i] // 16, (ctx[i] + depths[i]) // 16
+        for j, blk in enumerate(range(first, last + 1)):
+            wb_regions.append(tr.CopyRegion(ext, int(bt[i, blk]), j, 1))
+        off += wb_blocks
+    wb_plan = tr.CopyPlan("D2H", tuple(wb_regions))
+    restore_bytes = 2 * sum(restore_blocks) * block_bytes
+    be = NativeCopyBackend(arena=arena, k_cache=b.k_cache, v_cache=b.v_cache)
+    be.initialize()
+    wb = be.fork()
+    wb.initialize()
+    comp = torch.cuda.current_stream(dev)
+
+    def verify_round():
+        paged_attention_raw(qa, b.k_cache, b.v_cache, b.block_table, lens_a, ids_a, 0, scale, oa,
+                            max_len=max(b.seq_lens_list[ra:]))
+
+    for _ in range(3):
+        verify_round()
+    be.launch(restore_plan).synchronize()
+    torch.cuda.synchronize()
+    # 1. attention alone
+    steps = max(args.steps, 10)
+    ms_alone = _time_steps(verify_round, steps)
+    # 2. restore alone
+    t = be.launch(restore_plan)
+    t.synchronize()
+    restore_alone = restore_bytes / (t.duration_ms() * 1e-3) / 1e9
+    # 3. both: verify rounds (each followed by its writeback) until the restore is done
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t = be.launch(restore_plan)
+    e0.record(comp)
+    rounds = 0
+    while True:
+        verify_round()
+        ready = torch.cuda.Event()
+        ready.record(comp)
+        wb.launch(tr.CopyPlan("D2H", wb_plan.regions, dependencies=(ready,)))
+        rounds += 1
+        if rounds >= 4 and t.query():
+            break
+        if rounds > 20000:
+            break
+    e1.record(comp)
+    t.synchronize()
+    torch.cuda.synchronize()
+    ms_both = e0.elapsed_time(e1) / rounds
+    restore_both = restore_bytes / (t.duration_ms() * 1e-3) / 1e9
+    # bytes check: the restored GPU blocks equal the arena (both planes, a sample of blocks)
+    plane = arena.descriptor.plane_bytes
+    ok = True
+    for r_ in regions[:: max(1, len(regions) // 64)]:
+        hb = (r_.extent.offset_blocks + r_.host_begin_block) * block_bytes
+        g = b.k_cache[r_.gpu_begin_block].view(torch.uint8).cpu().numpy().reshape(-1)
+        ok &= bool((g == host[hb:hb + block_bytes]).all())
+        g = b.v_cache[r_.gpu_begin_block].view(torch.uint8).cpu().numpy().reshape(-1)
+        ok &= bool((g == host[plane + hb:plane + hb + block_bytes]).all())
+    wb.close()
+    be.close()
+    del host
+    arena.close()
+    arena.unlink()
+    peak, peak_kind = _peaks()
+    tb_alone = a_bytes / (ms_alone * 1e-3) / 1e12
+    tb_both = a_bytes / (ms_both * 1e-3) / 1e12
+    line = {"metric": metric, "value": round(tb_both, 4), "unit": "TB/s", "n_gpus": 1, "steps": rounds,
+            "warmup": 3, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+            "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": args.workload, "requests": nreq, "restoring": nb_restore,
+                       "verifying": nreq - nb_restore, "depth": cfg["depth"], "ctx": [cfg["ctx_lo"], cfg["ctx_hi"]],
+                       "restore_regions": len(regions), "restore_bytes": restore_bytes,
+                       "writeback_bytes_per_round": 2 * len(wb_regions) * block_bytes,
+                       "arena": "reference SharedHostKVArena (POSIX shared memory)"},
+            "attention_alone": {"tb_s": round(tb_alone, 4), "frac_of_measured_peak": round(tb_alone * 1e3 / peak, 4),
+                                "launch_us": round(ms_alone * 1e3, 2)},
+            "attention_during_restore": {"tb_s": round(tb_both, 4), "launch_us": round(ms_both * 1e3, 2),
+                                         "rounds": rounds},
+            "restore_gbs": {"alone": round(restore_alone, 2), "during_attention": round(restore_both, 2),
+                            "mode": be.mode},
+            "restored_bytes_match_arena": ok,
+            "roofline": {"bound": "hbm", "achieved": round(tb_both * 1e3, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(tb_both * 1e3 / peak, 4), "peak_kind": peak_kind}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
-    if args.workload == "greedy_accept_8b":
+    if args.workload.endswith("_hostkv"):
+        run_long_hostkv(args)
+    elif args.workload == "greedy_accept_8b":
         run_accept(args)
     elif args.workload == "fused_store_0p6b":
         run_fused(args)

@@ -17,6 +17,10 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 int check_cuda(cudaError_t e, const char* what) {
+  // The failure is reported through the return code; clear the runtime's
+  // record of it (non-sticky errors only), so that a later launch check on
+  // this thread does not report it again.
+  (void)cudaGetLastError();
   return set_error(NEB_ERR_CUDA, "%s failed: %s (%d)", what, cudaGetErrorString(e), (int)e);
 }
 

@@ -47,22 +47,39 @@ class NativeCopyTicket:
 
 
 class _OwnRegistration:
-    """cudaHostRegister(PORTABLE | MAPPED) when the caller supplies no registration pool."""
+    """cudaHostRegister(PORTABLE | MAPPED) when the caller supplies no registration pool.
+
+    Counted per arena address, so that a backend and its forks (which share
+    the registration, as the reference's ``fork`` does) register the arena
+    once and unregister it when the last of them closes."""
+
+    _lock = __import__("threading").Lock()
+    _count: dict[int, int] = {}
 
     def acquire(self, arena):
-        cudart = torch.cuda.cudart()
-        status = cudart.cudaHostRegister(arena.address(), arena.descriptor.total_bytes, 3)
-        code = int(status[0] if isinstance(status, tuple) else status)
-        if code != 0:
-            raise RuntimeError(f"cudaHostRegister failed with CUDA status {code}")
-        return arena.address()
+        address = arena.address()
+        with self._lock:
+            if self._count.get(address, 0) == 0:
+                cudart = torch.cuda.cudart()
+                status = cudart.cudaHostRegister(address, arena.descriptor.total_bytes, 3)
+                code = int(status[0] if isinstance(status, tuple) else status)
+                if code != 0:
+                    raise RuntimeError(f"cudaHostRegister failed with CUDA status {code}")
+            self._count[address] = self._count.get(address, 0) + 1
+        return address
 
     def release(self, record) -> None:
-        cudart = torch.cuda.cudart()
-        status = cudart.cudaHostUnregister(record)
-        code = int(status[0] if isinstance(status, tuple) else status)
-        if code != 0:
-            raise RuntimeError(f"cudaHostUnregister failed with CUDA status {code}")
+        with self._lock:
+            left = self._count.get(record, 0) - 1
+            if left > 0:
+                self._count[record] = left
+                return
+            self._count.pop(record, None)
+            cudart = torch.cuda.cudart()
+            status = cudart.cudaHostUnregister(record)
+            code = int(status[0] if isinstance(status, tuple) else status)
+            if code != 0:
+                raise RuntimeError(f"cudaHostUnregister failed with CUDA status {code}")
 
 
 def plan_regions(plan, arena, gpu_blocks: int) -> np.ndarray:

@@ -140,3 +140,26 @@ def test_migration_matches_writeback_then_restore(mode, cuda):
     oracle.migrate(src, exp, regions, bb)
     assert np.array_equal(dk.view(torch.uint8).cpu().numpy().reshape(-1), exp[0])
     assert np.array_equal(dv.view(torch.uint8).cpu().numpy().reshape(-1), exp[1])
+
+
+def test_fork_shares_its_own_registration(cuda):
+    """A backend that registered the arena itself and its fork (the second
+    bank's stream) share that registration: both copy, the arena is
+    registered once and unregistered when the last of them closes."""
+    from nebulasd_b200.hostkv import NativeCopyBackend, host_device_pointer
+    batch, blocks = 3, 2
+    k, v, arena, extents, cap, bb = _setup(batch, blocks, cuda)
+    be = NativeCopyBackend(arena=arena, k_cache=k, v_cache=v, mode="kernel")
+    be.initialize()
+    other = be.fork()
+    other.initialize()
+    for it, (backend, direction) in enumerate(((be, "H2D"), (other, "D2H"), (other, "H2D"), (be, "D2H"))):
+        plan = CopyPlan(direction, tuple(CopyRegion(e, i * cap + 1, 1, blocks) for i, e in enumerate(extents)))
+        _fill(arena, extents, k, v, cap, blocks, direction, it)
+        torch.cuda.synchronize()
+        backend.launch(plan).synchronize()
+        _check(arena, extents, k, v, cap, blocks, it)
+    be.close()
+    assert host_device_pointer(arena.address()) is not None  # the fork still holds it
+    other.close()
+    assert host_device_pointer(arena.address()) is None
