@@ -262,6 +262,7 @@ def run_ours(args):
         secondary["fused_qk_norm_rope_store_0p6b"] = _guard(lambda: fused_bar(dev))
         secondary["long_verify_8b_k4"] = _guard(lambda: secondary_attention("long_verify_8b_k4", dev, 3))
         secondary["long_verify_8b_k8"] = _guard(lambda: secondary_attention("long_verify_8b_k8", dev, 3))
+        secondary["long_verify_8b_k4_hostkv"] = _guard(lambda: long_hostkv_line("long_verify_8b_k4", dev, 10))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -910,28 +911,32 @@ def run_accept(args):
 
 
 def run_long_hostkv(args):
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    line = long_hostkv_line(args.workload.replace("_hostkv", ""), torch.device("cuda", local), args.steps,
+                            args.requests)
+    line["config"]["workload"] = args.workload
+    print(json.dumps(line), flush=True)
+
+
+def long_hostkv_line(workload, dev, steps_arg, requests=None):
     """Config 4 with its HostKV traffic (rank 0): 64 requests, ctx U[8K, 32K];
     bank B (a quarter of the requests) restores its full KV from the pinned
     host arena through NativeCopyBackend while bank A (the rest) runs
     long-context verify, and every verify round writes bank A's changed blocks
     (the k+1 new tokens) back on a second backend stream (``fork``).  The arena,
     extents and plans are the reference's (``SharedHostKVArena``, ``CopyPlan``)."""
-    world, rank, local = _dist()
-    if rank != 0:
-        return
     import numpy as np
     from baseline import reference as R
     from nebulasd_b200.hostkv import NativeCopyBackend
     from nebulasd_b200.kernels import paged_attention_raw
-    workload = args.workload.replace("_hostkv", "")
     metric = f"long-context verify TB/s with HostKV restore overlapped ({workload})"
     if not R.available():
-        print(json.dumps({"metric": metric, "unavailable": "reference not installed under baseline/_ref"}), flush=True)
-        return
+        return {"metric": metric, "unavailable": "reference not installed under baseline/_ref", "config": {}}
     arena_mod, tr = R.nebulasd("kv.arena"), R.nebulasd("kv.transfer")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    b, layers, cfg = build_workload(workload, 1234, dev, None, args.requests)
+    b, layers, cfg = build_workload(workload, 1234, dev, None, requests)
     nreq = cfg["num_requests"]
     nb_restore = nreq // 4
     bt = b.block_table.cpu().numpy()
@@ -954,8 +959,7 @@ def run_long_hostkv(args):
         arena = arena_mod.SharedHostKVArena.create(total_blocks=total_host, block_bytes=block_bytes,
                                                    dtype=str(b.k_cache.dtype), kv_block_shape=kv_shape)
     except OSError as e:
-        print(json.dumps({"metric": metric, "unavailable": f"shared-memory arena: {e}"}), flush=True)
-        return
+        return {"metric": metric, "unavailable": f"shared-memory arena: {e}", "config": {}}
     host = np.ctypeslib.as_array((__import__("ctypes").c_uint8 * arena.descriptor.total_bytes)
                                  .from_address(arena.address()))
     host[:] = np.random.default_rng(7).integers(0, 256, host.shape[0], dtype=np.uint8)
@@ -998,12 +1002,13 @@ def run_long_hostkv(args):
     be.launch(restore_plan).synchronize()
     torch.cuda.synchronize()
     # 1. attention alone
-    steps = max(args.steps, 10)
+    steps = max(steps_arg, 10)
     ms_alone = _time_steps(verify_round, steps)
     # 2. restore alone
     t = be.launch(restore_plan)
     t.synchronize()
     restore_alone = restore_bytes / (t.duration_ms() * 1e-3) / 1e9
+    restore_mode = be.last_mode
     # 3. both: verify rounds (each followed by its writeback) until the restore is done
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1045,7 +1050,7 @@ def run_long_hostkv(args):
     line = {"metric": metric, "value": round(tb_both, 4), "unit": "TB/s", "n_gpus": 1, "steps": rounds,
             "warmup": 3, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
             "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
-            "config": {"workload": args.workload, "requests": nreq, "restoring": nb_restore,
+            "config": {"workload": workload + "_hostkv", "requests": nreq, "restoring": nb_restore,
                        "verifying": nreq - nb_restore, "depth": cfg["depth"], "ctx": [cfg["ctx_lo"], cfg["ctx_hi"]],
                        "restore_regions": len(regions), "restore_bytes": restore_bytes,
                        "writeback_bytes_per_round": 2 * len(wb_regions) * block_bytes,
@@ -1055,11 +1060,13 @@ def run_long_hostkv(args):
             "attention_during_restore": {"tb_s": round(tb_both, 4), "launch_us": round(ms_both * 1e3, 2),
                                          "rounds": rounds},
             "restore_gbs": {"alone": round(restore_alone, 2), "during_attention": round(restore_both, 2),
-                            "mode": be.mode},
+                            "mode": restore_mode},
             "restored_bytes_match_arena": ok,
             "roofline": {"bound": "hbm", "achieved": round(tb_both * 1e3, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(tb_both * 1e3 / peak, 4), "peak_kind": peak_kind}}
-    print(json.dumps(line), flush=True)
+    k_cache_free(b)
+    torch.cuda.empty_cache()
+    return line
 
 
 def main():

@@ -13,7 +13,12 @@ per plan (``choose_copy_mode``): the copy engines for plans of long runs, where
 they reach the PCIe roofline (55.6 GB/s on B200, against 51 GB/s for the
 kernel), the single-launch kernel for plans of many short runs, where one
 driver call per run and plane would dominate; the kernel needs the arena
-mapped into the device address space.
+mapped into the device address space.  A restore whose arena ranges are long
+but whose GPU blocks are scattered (a request's KV into a paged pool) goes
+``mode="staged"``: the copy engines move the ranges into a device staging
+buffer and a device-to-device kernel scatters the blocks, so the restore holds
+no SM while it waits on the host link and the attention of the other bank
+keeps its speed.
 
 ``migrate_blocks`` is same-role migration as a direct peer copy over NVLink: the
 destination GPU's kernel reads the source GPU's cache through its unified
@@ -112,14 +117,63 @@ def merged_runs(regions: np.ndarray) -> int:
     return int(len(regions) - np.count_nonzero(cont))
 
 
-def choose_copy_mode(regions: np.ndarray, block_bytes: int, mapped: bool) -> str:
-    """``memcpy`` when the plan's runs average ``ENGINE_RUN_BYTES`` or more per plane, else ``kernel``."""
-    if not mapped:
-        return "memcpy"
+def host_runs(regions: np.ndarray) -> int:
+    """Runs of regions adjacent in the arena (whatever their GPU blocks)."""
+    if len(regions) == 0:
+        return 0
+    host, count = regions[:, 0], regions[:, 2]
+    return int(len(regions) - np.count_nonzero(host[1:] == host[:-1] + count[:-1]))
+
+
+# Device staging buffer of the staged restore, per plane and buffer (two buffers).
+STAGING_BYTES = 64 << 20
+
+
+def choose_copy_mode(regions: np.ndarray, block_bytes: int, mapped: bool, direction: str = "H2D") -> str:
+    """Per plan: ``memcpy`` when its runs (adjacent on both sides) average
+    ``ENGINE_RUN_BYTES`` or more per plane; for a restore whose arena ranges
+    are that long but whose GPU blocks are scattered (a request's KV into a
+    paged pool), ``staged``: the copy engines move the arena ranges into a
+    device staging buffer and a device-to-device kernel scatters the blocks,
+    so the restore holds no SM while it waits on the host link; else
+    ``kernel`` (the arena must be mapped) or ``memcpy``."""
     runs = merged_runs(regions)
     if runs == 0:
-        return "kernel"
-    return "memcpy" if int(regions[:, 2].sum()) * block_bytes >= ENGINE_RUN_BYTES * runs else "kernel"
+        return "kernel" if mapped else "memcpy"
+    total = int(regions[:, 2].sum()) * block_bytes
+    if total >= ENGINE_RUN_BYTES * runs:
+        return "memcpy"
+    if direction == "H2D" and total >= ENGINE_RUN_BYTES * host_runs(regions):
+        return "staged"
+    return "kernel" if mapped else "memcpy"
+
+
+def staged_pieces(regions: np.ndarray, capacity: int):
+    """Cut a restore plan into pieces of at most ``capacity`` blocks: per piece
+    the arena-to-staging regions and the staging-to-cache regions, both as
+    ``(src_block, dst_block, count)`` rows in plan order."""
+    if len(regions) == 0:
+        return []
+    host, gpu, count = regions[:, 0], regions[:, 1], regions[:, 2]
+    end = np.cumsum(count)
+    begin = end - count
+    # A region crossing a piece boundary is cut there: one row per (region, piece).
+    first, last = begin // capacity, (end - 1) // capacity
+    reps = last - first + 1
+    idx = np.repeat(np.arange(len(regions)), reps)
+    piece = np.repeat(first, reps) + (np.arange(reps.sum()) - np.repeat(np.cumsum(reps) - reps, reps))
+    lo = np.maximum(begin[idx], piece * capacity)
+    hi = np.minimum(end[idx], (piece + 1) * capacity)
+    src = host[idx] + (lo - begin[idx])
+    dst = gpu[idx] + (lo - begin[idx])
+    n = hi - lo
+    slot = lo - piece * capacity
+    bounds = np.flatnonzero(np.diff(piece)) + 1
+    out = []
+    for sel in np.split(np.arange(len(piece)), bounds):
+        out.append((np.stack([src[sel], slot[sel], n[sel]], 1).astype(np.int64),
+                    np.stack([slot[sel], dst[sel], n[sel]], 1).astype(np.int64)))
+    return out
 
 
 def host_device_pointer(host_address: int) -> int | None:
@@ -143,8 +197,8 @@ class NativeCopyBackend:
         if (arena.descriptor.dtype != str(k_cache.dtype)
                 or tuple(arena.descriptor.kv_block_shape) != tuple(k_cache.shape[1:])):
             raise ValueError("HostKV dtype/block shape does not match GPU layout")
-        if mode not in ("auto", "kernel", "memcpy"):
-            raise ValueError("mode must be auto, kernel or memcpy")
+        if mode not in ("auto", "kernel", "memcpy", "staged"):
+            raise ValueError("mode must be auto, kernel, memcpy or staged")
         self.arena = arena
         self.k_cache, self.v_cache = k_cache, v_cache
         self._device = k_cache.device
@@ -155,6 +209,9 @@ class NativeCopyBackend:
             self._registration = _PoolAdapter(registration)
         self._record = None
         self._stream = None
+        self._scatter_stream = None
+        self._staging = None
+        self.last_mode = None  # the mode the last launch used
         self._host_base = None  # address the copy uses for the arena (device-mapped or host)
         self._mapped = None     # device address of the arena, when it is mapped
         self.mode = None
@@ -176,13 +233,15 @@ class NativeCopyBackend:
         if self._registration is None:
             self._registration = _OwnRegistration()
         self._stream = torch.cuda.Stream(device=self._device)
+        self._scatter_stream = torch.cuda.Stream(device=self._device)
         self._record = self._registration.acquire(self.arena)
         mapped = host_device_pointer(self.arena.address())
         if self._mode_request == "kernel" and mapped is None:
             raise RuntimeError("kernel copies need the HostKV arena mapped into the device address space")
         self._mapped = mapped
-        if self._mode_request == "memcpy" or mapped is None:
-            self.mode, self._host_base = "memcpy", self.arena.address()
+        if self._mode_request in ("memcpy", "staged") or mapped is None:
+            self.mode, self._host_base = self._mode_request if self._mode_request != "auto" else "memcpy", \
+                self.arena.address()
         else:
             self.mode, self._host_base = "kernel", mapped
 
@@ -193,9 +252,12 @@ class NativeCopyBackend:
         regions = plan_regions(plan, self.arena, self.k_cache.shape[0])
         d = self.arena.descriptor
         mode, host_base = self.mode, self._host_base
-        if self._mode_request == "auto" and self._mapped is not None:
-            mode = choose_copy_mode(regions, d.block_bytes, True)
-            host_base = self._mapped if mode == "kernel" else self.arena.address()
+        if self._mode_request == "auto":
+            mode = choose_copy_mode(regions, d.block_bytes, self._mapped is not None, plan.direction)
+        if mode == "staged" and plan.direction != "H2D":  # writebacks: the direct path
+            mode = "kernel" if self._mapped is not None else "memcpy"
+        self.last_mode = mode
+        host_base = self._mapped if mode == "kernel" else self.arena.address()
         with torch.cuda.stream(self._stream):
             for dependency in plan.dependencies:
                 if hasattr(dependency, "query") and hasattr(dependency, "record"):
@@ -203,7 +265,9 @@ class NativeCopyBackend:
             start = torch.cuda.Event(enable_timing=True)
             done = torch.cuda.Event(enable_timing=True, blocking=True)
             start.record(self._stream)
-            if len(regions):
+            if len(regions) and mode == "staged":
+                self._staged_restore(regions, host_base)
+            elif len(regions):
                 rc = _lib.lib.neb_hostkv_copy(
                     1 if plan.direction == "H2D" else 0, host_base + d.k_plane_offset,
                     host_base + d.v_plane_offset, self.k_cache.data_ptr(), self.v_cache.data_ptr(),
@@ -212,6 +276,37 @@ class NativeCopyBackend:
                 _lib.check(rc, "neb_hostkv_copy")
             done.record(self._stream)
         return NativeCopyTicket(start, done)
+
+    def _staged_restore(self, regions: np.ndarray, host_base: int) -> None:
+        """Arena ranges -> staging buffer (copy engines, backend stream) ->
+        cache blocks (copy kernel, scatter stream), two buffers in flight; the
+        backend stream waits for the last scatter."""
+        d = self.arena.descriptor
+        bb = d.block_bytes
+        cap = max(1, STAGING_BYTES // bb)
+        if self._staging is None:
+            with torch.inference_mode(False):
+                self._staging = torch.empty((2, 2, cap * bb), dtype=torch.uint8, device=self._device)
+        scattered = []
+        for i, (dma, scatter) in enumerate(staged_pieces(regions, cap)):
+            buf = self._staging[i % 2]
+            if i >= 2:
+                self._stream.wait_event(scattered[i - 2])
+            rc = _lib.lib.neb_hostkv_copy(1, host_base + d.k_plane_offset, host_base + d.v_plane_offset,
+                                          buf[0].data_ptr(), buf[1].data_ptr(), bb, dma.ctypes.data, len(dma),
+                                          MODES["memcpy"], self._stream.cuda_stream)
+            _lib.check(rc, "neb_hostkv_copy")
+            landed = torch.cuda.Event()
+            landed.record(self._stream)
+            self._scatter_stream.wait_event(landed)
+            rc = _lib.lib.neb_kv_peer_copy(buf[0].data_ptr(), buf[1].data_ptr(), self.k_cache.data_ptr(),
+                                           self.v_cache.data_ptr(), bb, scatter.ctypes.data, len(scatter),
+                                           MODES["kernel"], self._scatter_stream.cuda_stream)
+            _lib.check(rc, "neb_kv_peer_copy")
+            ev = torch.cuda.Event()
+            ev.record(self._scatter_stream)
+            scattered.append(ev)
+        self._stream.wait_event(scattered[-1])
 
     def close(self) -> None:
         if self._close_error is not None:
@@ -222,13 +317,14 @@ class NativeCopyBackend:
         try:
             if self._stream is not None:
                 self._stream.synchronize()
+                self._scatter_stream.synchronize()
             if self._record is not None:
                 self._registration.release(self._record)
                 self._record = None
         except BaseException as error:  # keep the reference's close-error contract
             self._close_error = error
             raise
-        self._stream = None
+        self._stream = self._scatter_stream = self._staging = None
         self.k_cache = self.v_cache = None
 
 

@@ -96,7 +96,7 @@ def test_op_modules_import_without_gpu():
 def test_copy_mode_choice_by_run_length():
     """auto mode: copy engines for long runs, the single-launch kernel for many short ones."""
     import numpy as np
-    from nebulasd_b200.hostkv import ENGINE_RUN_BYTES, choose_copy_mode, merged_runs
+    from nebulasd_b200.hostkv import ENGINE_RUN_BYTES, choose_copy_mode, host_runs, merged_runs
     block = 1_179_648  # Qwen3-8B HostKV block (36 layers x 8 kv heads x 16 x 128 x 2 B)
     long_runs = np.array([[0, 200, 253], [253, 453, 252]], dtype=np.int64)
     assert merged_runs(long_runs) == 1  # adjacent on both sides: one run per plane
@@ -108,6 +108,32 @@ def test_copy_mode_choice_by_run_length():
     assert choose_copy_mode(short, block, mapped=True) == "memcpy"  # 1.18 MB per run is long enough
     assert choose_copy_mode(short, 4096, mapped=False) == "memcpy"  # unmapped arena: engines only
     assert choose_copy_mode(np.zeros((0, 3), dtype=np.int64), block, mapped=True) == "kernel"
+    # A request's KV restored into a paged pool: one arena range, scattered GPU blocks.
+    restore = np.stack([np.arange(256), np.arange(256) * 7 % 1021, np.ones(256, dtype=np.int64)], 1)
+    assert host_runs(restore) == 1 and merged_runs(restore) == 256
+    assert choose_copy_mode(restore, 32768, mapped=True) == "staged"
+    assert choose_copy_mode(restore, 32768, mapped=False) == "staged"
+    assert choose_copy_mode(restore, 32768, mapped=True, direction="D2H") == "kernel"  # writebacks: direct
+    assert choose_copy_mode(restore[:16], 32768, mapped=True) == "kernel"  # 512 KB in all: too short to stage
+
+
+def test_staged_pieces_cover_the_plan_within_capacity():
+    import numpy as np
+    from nebulasd_b200.hostkv import staged_pieces
+    rng = np.random.default_rng(3)
+    counts = rng.integers(1, 9, 50)
+    host = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    gpu = rng.permutation(2000)[:50] * 10
+    regions = np.stack([host, gpu, counts], 1).astype(np.int64)
+    pieces = staged_pieces(regions, 16)
+    moved = []
+    for dma, scatter in pieces:
+        assert (dma[:, 2] == scatter[:, 2]).all() and dma[:, 2].sum() <= 16
+        assert (dma[:, 1] == scatter[:, 0]).all()
+        for (h, sb, n), (_, g, _) in zip(dma.tolist(), scatter.tolist()):
+            moved += [(h + j, g + j) for j in range(n)]
+    want = [(h + j, g + j) for h, g, n in regions.tolist() for j in range(n)]
+    assert moved == want
 
 
 def test_greedy_accept_rejects_bad_arguments_on_the_host():
