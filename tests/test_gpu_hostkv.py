@@ -55,7 +55,7 @@ def _check(arena, extents, k, v, cap, blocks, it):
             assert (gpu[:bb] == 204).all() and (gpu[-bb:] == 204).all(), "GPU guard overwritten"
 
 
-@pytest.mark.parametrize("mode", ["kernel", "memcpy"])
+@pytest.mark.parametrize("mode", ["kernel", "memcpy", "staged"])
 def test_copy_backend_guard_blocks(mode, cuda):
     from nebulasd_b200.hostkv import NativeCopyBackend
     batch, blocks = 5, 3
@@ -75,7 +75,7 @@ def test_copy_backend_guard_blocks(mode, cuda):
         backend.close()
 
 
-@pytest.mark.parametrize("mode", ["kernel", "memcpy"])
+@pytest.mark.parametrize("mode", ["kernel", "memcpy", "staged"])
 def test_random_regions_match_oracle(mode, cuda):
     from nebulasd_b200.hostkv import NativeCopyBackend
     rng = np.random.default_rng(5)
@@ -163,3 +163,35 @@ def test_fork_shares_its_own_registration(cuda):
     assert host_device_pointer(arena.address()) is not None  # the fork still holds it
     other.close()
     assert host_device_pointer(arena.address()) is None
+
+
+def test_staged_restore_in_small_pieces(cuda, monkeypatch):
+    """The staged restore cut into many 3-block pieces (both staging buffers
+    reused over and over) leaves the same bytes as the oracle."""
+    from nebulasd_b200 import hostkv
+    rng = np.random.default_rng(9)
+    nb = 64
+    k = torch.zeros((nb, *SHAPE), dtype=torch.float16, device=cuda)
+    v = torch.zeros_like(k)
+    bb = k[0].numel() * 2
+    monkeypatch.setattr(hostkv, "STAGING_BYTES", 3 * bb)
+    arena = Arena(96, bb, dtype=str(k.dtype), kv_block_shape=SHAPE)
+    hk, hv = arena.planes()
+    hk[:] = rng.integers(0, 256, hk.shape, dtype=np.uint8)
+    hv[:] = rng.integers(0, 256, hv.shape, dtype=np.uint8)
+    ext = arena.make_extent(4, 60)
+    dst = rng.permutation(nb)[:40]  # 40 one-block regions of one arena range, scattered GPU blocks
+    regions = tuple(CopyRegion(ext, int(g), j, 1) for j, g in enumerate(dst))
+    backend = hostkv.NativeCopyBackend(arena=arena, k_cache=k, v_cache=v, mode="staged")
+    try:
+        gpu_before = (k.view(torch.uint8).cpu().numpy().reshape(-1).copy(),
+                      v.view(torch.uint8).cpu().numpy().reshape(-1).copy())
+        host_before = (hk.copy(), hv.copy())
+        backend.launch(CopyPlan("H2D", regions)).synchronize()
+        assert backend.last_mode == "staged"
+        triples = [(ext.offset_blocks + r.host_begin_block, r.gpu_begin_block, r.block_count) for r in regions]
+        oracle.apply_regions("H2D", triples, host_before, gpu_before, bb)
+        assert np.array_equal(k.view(torch.uint8).cpu().numpy().reshape(-1), gpu_before[0])
+        assert np.array_equal(v.view(torch.uint8).cpu().numpy().reshape(-1), gpu_before[1])
+    finally:
+        backend.close()
