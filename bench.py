@@ -1069,9 +1069,144 @@ def long_hostkv_line(workload, dev, steps_arg, requests=None):
     return line
 
 
+class _B200Ops:
+    """``nebulasd_b200.install()`` for one block, then the reference's ops back."""
+
+    def __init__(self, R):
+        self.layer_mod = R.swiftllm("worker.layers.transformer_layer")
+        names = (("paged_attention", "paged_attn"), ("store_kvcache", "kvcache_mgmt"),
+                 ("rotary_embedding_inplace", "rotary_emb"), ("rmsnorm_inplace", "rmsnorm"))
+        self.kernel_mods = {n: R.swiftllm(f"worker.kernels.{m}") for n, m in names}
+        self.saved = {n: (getattr(self.layer_mod, n), getattr(self.kernel_mods[n], n)) for n, _ in names}
+        self.copy_mod = sys.modules.get("nebulasd.kv.cuda_transfer")
+        self.copy_backend = getattr(self.copy_mod, "CudaCopyBackend", None)
+
+    def __enter__(self):
+        import nebulasd_b200
+        nebulasd_b200.install()
+        return self
+
+    def __exit__(self, *exc):
+        for n, (layer_fn, mod_fn) in self.saved.items():
+            setattr(self.layer_mod, n, layer_fn)
+            setattr(self.kernel_mods[n], n, mod_fn)
+        if self.copy_mod is not None:
+            self.copy_mod.CudaCopyBackend = self.copy_backend
+        return False
+
+
+def run_spec_e2e(args):
+    """Config 5 reduced to one GPU: greedy speculative decoding (depth 4) of
+    16 requests (prompts of U[128, 1024] random token ids) by a random-init
+    Qwen3-0.6B Draft and Qwen3-8B Target, both the reference's own
+    ``LlamaModel`` (``swiftLLM/swiftllm/worker/model.py``) on one B200, each
+    round: the Draft catches up on the committed tokens and proposes 4, the
+    Target verifies the 5 rows per request, ``compute_greedy_acceptance``
+    (``speculative.py:122-156``) commits.  Run twice, with the reference's
+    kernels and after ``nebulasd_b200.install()``; reports tokens/s and the
+    share of the rounds' time spent in paged attention."""
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    import random
+    import tempfile
+    from baseline import reference as R
+    metric = "speculative decoding tokens/s (random-init Qwen3-0.6B Draft + Qwen3-8B Target, one B200, depth 4)"
+    if not R.available():
+        print(json.dumps({"metric": metric, "unavailable": "reference not installed under baseline/_ref"}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    spec = R.swiftllm("speculative")
+    reqs, depth, rounds = args.requests or 16, 4, max(args.steps, 8)
+    rng = random.Random(2026)
+    prompts = [[rng.randrange(151936) for _ in range(rng.randint(128, 1024))] for _ in range(reqs)]
+    mbs = (1024 + (rounds + 2) * (depth + 1)) // 16 + 2
+    tmp = tempfile.mkdtemp(prefix="neb_spec_")
+    kw = dict(max_seqs=reqs, max_blocks_per_seq=mbs, num_blocks=reqs * mbs, max_batch=reqs * (depth + 2) * 4,
+              max_tokens=sum(len(p) for p in prompts) + 64)
+    draft = R.random_llama(R.QWEN3_0P6B, tmp + "/draft", 1, **kw)
+    target = R.random_llama(R.QWEN3_8B, tmp + "/target", 2, **kw)
+    bt = torch.arange(reqs * mbs, dtype=torch.int32, device="cuda").view(reqs, mbs).contiguous()
+    ids = list(range(reqs))
+    layer_mod = R.swiftllm("worker.layers.transformer_layer")
+
+    def arm():
+        attn = []
+        inner = layer_mod.paged_attention
+
+        def timed(*a, **k):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            inner(*a, **k)
+            e1.record()
+            attn.append((e0, e1))
+
+        layer_mod.paged_attention = timed
+        try:
+            committed = [list(p) for p in prompts]
+            first = target.forward(prompts, ids, [], kv_block_table=bt)
+            draft.forward(prompts, ids, [], kv_block_table=bt)
+            for r in ids:
+                committed[r].append(first[r])
+            draft_len = [len(p) for p in prompts]
+            torch.cuda.synchronize()
+            attn.clear()
+            t0 = time.perf_counter()
+            for _ in range(rounds):
+                rows, rids, lens, last = [], [], [], []
+                for r in ids:  # the Draft catches up, then proposes
+                    for pos in range(draft_len[r], len(committed[r])):
+                        rows.append([committed[r][pos]])
+                        rids.append(r)
+                        lens.append(pos + 1)
+                    last.append(len(rows) - 1)
+                    draft_len[r] = len(committed[r])
+                out = draft.forward(rows, rids, lens, kv_block_table=bt)
+                drafts = [[out[i]] for i in last]
+                for j in range(1, depth):
+                    out = draft.forward([[d[-1]] for d in drafts], ids, [len(committed[r]) + j for r in ids],
+                                        kv_block_table=bt)
+                    for r in ids:
+                        drafts[r].append(out[r])
+                vrows = [[t] for r in ids for t in [committed[r][-1]] + drafts[r]]
+                vlens = [len(committed[r]) + i for r in ids for i in range(depth + 1)]
+                post = target.forward(vrows, [r for r in ids for _ in range(depth + 1)], vlens, kv_block_table=bt)
+                for r in ids:
+                    acc, _ = spec.compute_greedy_acceptance(drafts[r], post[r * (depth + 1):(r + 1) * (depth + 1)])
+                    committed[r] += acc
+            torch.cuda.synchronize()
+            secs = time.perf_counter() - t0
+            attn_ms = sum(a.elapsed_time(b) for a, b in attn)
+        finally:
+            layer_mod.paged_attention = inner
+        new = sum(len(c) - len(p) - 1 for c, p in zip(committed, prompts))
+        return {"tokens_per_s": round(new / secs, 1), "round_ms": round(secs * 1e3 / rounds, 3),
+                "attention_ms_per_round": round(attn_ms / rounds, 3),
+                "attention_share": round(attn_ms / (secs * 1e3), 4), "tokens": new}, committed
+
+    arm()  # warm-up: Triton JIT and the first calls of both models
+    ref, ref_tokens = arm()
+    with _B200Ops(R):
+        arm()
+        ours, our_tokens = arm()
+    same = sum(a == b for a, b in zip(ref_tokens, our_tokens))
+    line = {"metric": metric, "value": ours["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": rounds,
+            "warmup": 1, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic (random-init models, random prompt ids)",
+            "config": {"workload": "spec_decode_1d1t", "requests": reqs, "depth": depth,
+                       "prompt_len": [128, 1024], "rounds": rounds,
+                       "models": "Qwen3-0.6B Draft (28 layers) + Qwen3-8B Target (36 layers), random init"},
+            "ours": ours, "reference_kernels": ref,
+            "speedup": round(ours["tokens_per_s"] / ref["tokens_per_s"], 3),
+            "requests_with_identical_tokens": same}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
-    if args.workload.endswith("_hostkv"):
+    if args.workload == "spec_decode_1d1t":
+        run_spec_e2e(args)
+    elif args.workload.endswith("_hostkv"):
         run_long_hostkv(args)
     elif args.workload == "greedy_accept_8b":
         run_accept(args)

@@ -1,7 +1,8 @@
 """Device scratch for the attention kernels, one buffer per (device, stream).
 
 The split-K kernels keep per-unit arrival counters and per-slot fp32 partials
-in this buffer (the reference allocates its fp32 ``mid_o`` partials with
+in this buffer, and the verify kernel the work plan of its previous call (its
+plan cache: calls on one buffer must be ordered on one stream) (the reference allocates its fp32 ``mid_o`` partials with
 ``torch.empty`` on every call, ``swiftLLM/swiftllm/worker/kernels/paged_attn.py:170-180``).
 The counters must be zero when a call starts, and every call leaves them at
 zero, so a buffer is zero-filled once when it is created and then reused by

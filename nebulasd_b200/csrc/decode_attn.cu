@@ -184,6 +184,8 @@ template <int GQA>
 __global__ void __launch_bounds__(kDecodeThreads, (GQA <= 2 ? 4 : 2)) decode_attn_kernel(AttnParams p) {
   extern __shared__ int smem[];
   __shared__ int scratch[32];
+  pdl_trigger();
+  pdl_wait();  // inputs may come from the previous launch in the stream
   PlanSmem ps{smem, smem + (p.num_rows + 1), smem + 2 * (p.num_rows + 1), nullptr};
   build_plan(ps, scratch, p.seq_ids, p.seq_lens, p.num_rows, 1);
   const int ng = ps.misc[0];
@@ -248,14 +250,17 @@ int launch_decode(const AttnParams& p, long long workers, cudaStream_t stream) {
   const int grid = (int)(workers / kDecodeWarps);
   const size_t smem = plan_smem_bytes(p.num_rows);
   const int gqa = p.num_q_heads / p.num_kv_heads;
+  // Programmatic stream serialisation: the next launch is scheduled as this
+  // one starts, and each waits for its predecessor before reading any input,
+  // so the launch gap and the previous launch's tail overlap.
+  const dim3 g((unsigned)grid), b(kDecodeThreads);
   switch (gqa) {
-    case 1: decode_attn_kernel<1><<<grid, kDecodeThreads, smem, stream>>>(p); break;
-    case 2: decode_attn_kernel<2><<<grid, kDecodeThreads, smem, stream>>>(p); break;
-    case 4: decode_attn_kernel<4><<<grid, kDecodeThreads, smem, stream>>>(p); break;
-    case 8: decode_attn_kernel<8><<<grid, kDecodeThreads, smem, stream>>>(p); break;
+    case 1: NEB_CUDA(launch_pdl(decode_attn_kernel<1>, g, b, smem, stream, p)); break;
+    case 2: NEB_CUDA(launch_pdl(decode_attn_kernel<2>, g, b, smem, stream, p)); break;
+    case 4: NEB_CUDA(launch_pdl(decode_attn_kernel<4>, g, b, smem, stream, p)); break;
+    case 8: NEB_CUDA(launch_pdl(decode_attn_kernel<8>, g, b, smem, stream, p)); break;
     default: return set_error(NEB_ERR_UNSUPPORTED, "decode attention supports q/kv head ratios 1, 2, 4, 8 (got %d)", gqa);
   }
-  NEB_CUDA(cudaGetLastError());
   return NEB_OK;
 }
 

@@ -127,6 +127,8 @@ __device__ __forceinline__ uint2 norm_rope_row(const RopeStoreParams& p, const _
 
 // Items: per token, H q rows, then Hk k rows, then Hk v rows.
 __global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(RopeStoreParams p) {
+  pdl_trigger();  // the attention launch that follows may start its set-up
+  pdl_wait();     // q, k, v come from the previous launch (the QKV projection)
   const int lane = threadIdx.x & 31;
   const int d = (lane & 15) * 4 + (lane >> 4) * 64;
   const int per_tok = p.num_q_heads + 2 * p.num_kv_heads;
@@ -187,8 +189,7 @@ static int launch_rope_store(const RopeStoreParams& p, cudaStream_t stream) {
   if (items == 0) return NEB_OK;
   const long long blocks = (items + 7) / 8;
   const int grid = (int)(blocks < 65535 ? blocks : 65535);
-  qk_norm_rope_store_kernel<<<grid, 256, 0, stream>>>(p);
-  NEB_CUDA(cudaGetLastError());
+  NEB_CUDA(launch_pdl(qk_norm_rope_store_kernel, dim3((unsigned)grid), dim3(256), 0, stream, p));
   return NEB_OK;
 }
 
