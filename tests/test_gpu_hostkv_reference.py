@@ -136,3 +136,34 @@ def test_reference_backend_and_native_backend_agree(cuda):
         del host
         arena.close()
         arena.unlink()
+
+
+@pytest.mark.parametrize("mode", ["auto", "staged", "kernel"])
+def test_reference_dma_windows(mode, cuda):
+    """Restore plans cut by the reference DMA process's window policy
+    (``bounded_regions``, ``nebulasd/src/nebulasd/workers/dma_process.py:21-37``,
+    here a two-block window) run through NativeCopyBackend under the
+    reference's CopyExecutor leave the arena's bytes in the GPU blocks."""
+    from nebulasd_b200.hostkv import NativeCopyBackend
+    tr = R.nebulasd("kv.transfer")
+    dma = R.nebulasd("workers.dma_process")
+    batch, blocks = 4, 7
+    k, v, arena, extents, cap, bb = _setup(batch, blocks, cuda)
+    host = _host_bytes(arena)
+    plane_bytes = arena.descriptor.plane_bytes
+    backend = NativeCopyBackend(arena=arena, k_cache=k, v_cache=v, mode=mode)
+    executor = tr.CopyExecutor(backend, h2d_wait_mode="event")
+    try:
+        plan = tr.CopyPlan("H2D", tuple(tr.CopyRegion(e, i * cap + 1, 1, blocks) for i, e in enumerate(extents)))
+        windowed = dma.bounded_regions(plan, bb, 2 * 2 * bb)
+        assert len(windowed.regions) == batch * ((blocks + 1) // 2)
+        _fill(host, plane_bytes, k, v, cap, blocks, batch, bb, "H2D", 3)
+        torch.cuda.synchronize()
+        executor.submit(windowed).result(timeout=60)
+        torch.cuda.synchronize()
+        _check(host, plane_bytes, k, v, cap, blocks, batch, bb, 3)
+    finally:
+        executor.close()
+        del host
+        arena.close()
+        arena.unlink()
