@@ -288,7 +288,8 @@ def run_ours(args):
                      "bytes_per_launch": per_step // layers, "launch_us": round(launch_ms * 1e3, 3)},
         "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps, "api": "nebulasd_b200.kernels.paged_attention",
-                "copies": "per-layer q rows H2D and o rows D2H on two side streams, overlapped with attention"},
+                "copies": "each step's q rows, lengths and table H2D and its o rows D2H on two side streams, "
+                          "double-buffered so they overlap the neighbouring steps"},
         "requests_per_s": round(requests_per_s, 1),
         "strong_scaling": strong,
         "gpu_launches": args.steps * layers,
@@ -315,11 +316,12 @@ def measure_e2e(b, layers, dev, world, steps, scale, barrier):
     """Same metric through ``nebulasd_b200.kernels.paged_attention`` with HOST buffers.
 
     Every step copies its inputs from pinned host memory (the block table,
-    lengths and seq ids, then each layer's q rows) on an H2D stream and each
-    layer's o rows back on a D2H stream; attention of layer l waits only for
-    its own q rows, and the copy-out of layer l runs while layer l + 1 computes
-    (the pipelined host interface a serving loop would use).  The timed region
-    covers every copy.
+    lengths and seq ids, and all layers' q rows) on an H2D stream and reads
+    every layer's o rows back on a D2H stream, both inside the timed region.
+    The device buffers are doubled: step s + 1's inputs go up while step s
+    computes, and step s's outputs come down while step s + 1 computes (the
+    pipelined host interface of a serving loop); the timed region ends when
+    the last step's outputs are on the host.
     """
     from nebulasd_b200.kernels import paged_attention
     from nebulasd_b200.workloads import decode_infer_state
@@ -330,53 +332,56 @@ def measure_e2e(b, layers, dev, world, steps, scale, barrier):
     lens_host = b.seq_lens.cpu().pin_memory()
     ids_host = b.seq_ids.cpu().pin_memory()
     bt_host = b.block_table.cpu().pin_memory()
-    q_dev = torch.empty((layers, R, H, D), dtype=torch.float16, device=dev)
-    o_dev = torch.empty((layers, R, H * D), dtype=torch.float16, device=dev)
-    lens_dev, ids_dev, bt_dev = torch.empty_like(b.seq_lens), torch.empty_like(b.seq_ids), torch.empty_like(b.block_table)
-    st = decode_infer_state(lens_dev, ids_dev, b.seq_lens_list, b.num_kv_heads, scale)
+    bufs = []
+    for _ in range(2):
+        buf = types.SimpleNamespace(
+            q=torch.empty((layers, R, H, D), dtype=torch.float16, device=dev),
+            o=torch.empty((layers, R, H * D), dtype=torch.float16, device=dev),
+            lens=torch.empty_like(b.seq_lens), ids=torch.empty_like(b.seq_ids), bt=torch.empty_like(b.block_table),
+            ready=torch.cuda.Event(), used=torch.cuda.Event(), done=torch.cuda.Event(), drained=torch.cuda.Event())
+        buf.st = decode_infer_state(buf.lens, buf.ids, b.seq_lens_list, b.num_kv_heads, scale)
+        bufs.append(buf)
     mc = types.SimpleNamespace(num_q_heads=H, num_kv_heads=b.num_kv_heads, head_dim=D, num_layers=layers)
     ec = types.SimpleNamespace(block_size=16, max_blocks_per_seq=b.block_table.shape[1])
     comp = torch.cuda.current_stream(dev)
     h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev = lambda: torch.cuda.Event()  # noqa: E731
-    tables_ready, tables_used = ev(), ev()
-    q_ready, q_used = [ev() for _ in range(layers)], [ev() for _ in range(layers)]
-    o_ready, o_drained = [ev() for _ in range(layers)], [ev() for _ in range(layers)]
 
-    def e2e_step():
+    def upload(buf):
         with torch.cuda.stream(h2d_s):
-            h2d_s.wait_event(tables_used)  # the previous step's last layer is done with them
-            lens_dev.copy_(lens_host, non_blocking=True)
-            ids_dev.copy_(ids_host, non_blocking=True)
-            bt_dev.copy_(bt_host, non_blocking=True)
-            tables_ready.record(h2d_s)
-            for layer in range(layers):
-                h2d_s.wait_event(q_used[layer])
-                q_dev[layer].copy_(q_host[layer], non_blocking=True)
-                q_ready[layer].record(h2d_s)
-        comp.wait_event(tables_ready)
-        for layer in range(layers):
-            comp.wait_event(q_ready[layer])
-            comp.wait_event(o_drained[layer])
-            paged_attention(q_dev[layer], b.k_cache, b.v_cache, bt_dev, mc, ec, st, layer, o_dev[layer])
-            q_used[layer].record(comp)
-            o_ready[layer].record(comp)
-            with torch.cuda.stream(d2h_s):
-                d2h_s.wait_event(o_ready[layer])
-                o_host[layer].copy_(o_dev[layer], non_blocking=True)
-                o_drained[layer].record(d2h_s)
-        tables_used.record(comp)
+            h2d_s.wait_event(buf.used)  # the step that last read this buffer is done with it
+            buf.lens.copy_(lens_host, non_blocking=True)
+            buf.ids.copy_(ids_host, non_blocking=True)
+            buf.bt.copy_(bt_host, non_blocking=True)
+            buf.q.copy_(q_host, non_blocking=True)
+            buf.ready.record(h2d_s)
 
-    for _ in range(2):
-        e2e_step()
+    def compute(buf):
+        comp.wait_event(buf.ready)
+        comp.wait_event(buf.drained)  # the previous read-back of this buffer's outputs
+        for layer in range(layers):
+            paged_attention(buf.q[layer], b.k_cache, b.v_cache, buf.bt, mc, ec, buf.st, layer, buf.o[layer])
+        buf.used.record(comp)
+        buf.done.record(comp)
+        with torch.cuda.stream(d2h_s):
+            d2h_s.wait_event(buf.done)
+            o_host.copy_(buf.o, non_blocking=True)
+            buf.drained.record(d2h_s)
+
+    def run(n):
+        upload(bufs[0])
+        for i in range(n):
+            if i + 1 < n:
+                upload(bufs[(i + 1) % 2])
+            compute(bufs[i % 2])
+
+    run(2)
     torch.cuda.synchronize()
     barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(comp)
     h2d_s.wait_event(f0)
-    for _ in range(steps):
-        e2e_step()
-    comp.wait_event(o_drained[-1])
+    run(steps)
+    comp.wait_event(bufs[(steps - 1) % 2].drained)
     f1.record(comp)
     torch.cuda.synchronize()
     barrier()

@@ -53,9 +53,16 @@ def workspace_errors(buf: torch.Tensor, stream: torch.cuda.Stream) -> int:
     return bits.value
 
 
+# Bumped whenever buffers are dropped, so that callers keeping a reference to
+# the last buffer they used look it up again.
+generation = 0
+
+
 def release_all() -> None:
+    global generation
     with _lock:
         _buffers.clear()
+        generation += 1
 
 
 _error_words: dict[int, torch.Tensor] = {}

@@ -24,6 +24,7 @@ import os
 import torch
 
 from .. import _lib
+from .. import _workspace as _ws
 from .._workspace import attention_workspace
 
 _MODES = {"auto": None, "decode": _lib.NEB_ATTN_DECODE, "verify": _lib.NEB_ATTN_VERIFY,
@@ -75,6 +76,36 @@ def choose_kernel(num_q_heads: int, num_kv_heads: int, num_rows: int = 0, max_le
 
 _ENTRY = {}
 
+# The current stream's raw handle without building a Stream object (a host
+# cost of every call); torch.cuda.current_stream is the fallback.
+_raw_stream_fn = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _raw_stream(index: int) -> int:
+    if _raw_stream_fn is not None:
+        return _raw_stream_fn(index)
+    return torch.cuda.current_stream(index).cuda_stream
+
+
+# The workspace of the previous call, reused while the call's kernel, device,
+# stream and shape and the workspace generation stay the same (the 36 layer
+# calls of a forward).  One tuple, swapped as a whole, so threads never pair
+# one call's key with another's buffer.
+_last = (None, None)
+
+
+def _last_workspace(kernel, q, stream, stream_ptr, num_rows, num_q_heads, num_kv_heads):
+    global _last
+    idx = q.get_device()
+    key = (kernel, idx, stream_ptr, num_rows, num_q_heads, num_kv_heads, _ws.generation)
+    last_key, last_ws = _last
+    if key == last_key:
+        return last_ws
+    s = stream if stream is not None else torch.cuda.ExternalStream(stream_ptr, device=idx)
+    ws = attention_workspace(kernel, torch.device("cuda", idx), s, num_rows, num_q_heads, num_kv_heads)
+    _last = (key, ws)
+    return ws
+
 
 def _entry(kernel: int):
     if not _ENTRY:
@@ -84,14 +115,16 @@ def _entry(kernel: int):
     return _ENTRY[kernel]
 
 
+_F16, _I32 = torch.float16, torch.int32
+
+
 def _check_tensors(q, k_cache, v_cache, block_table, seq_lens, seq_ids, o):
-    if q.dtype != torch.float16 or k_cache.dtype != torch.float16 or v_cache.dtype != torch.float16 \
-            or o.dtype != torch.float16:
+    if q.dtype != _F16 or k_cache.dtype != _F16 or v_cache.dtype != _F16 or o.dtype != _F16:
         raise TypeError("q, k_cache, v_cache and o must be float16")
-    if block_table.dtype != torch.int32 or seq_lens.dtype != torch.int32 or seq_ids.dtype != torch.int32:
+    if block_table.dtype != _I32 or seq_lens.dtype != _I32 or seq_ids.dtype != _I32:
         raise TypeError("block_table, seq_lens and seq_ids must be int32")
-    dev = q.device
-    if dev.type != "cuda" or any(t.device != dev for t in (k_cache, v_cache, block_table, seq_lens, seq_ids, o)):
+    idx = q.get_device()  # -1 on the host
+    if idx < 0 or any(t.get_device() != idx for t in (k_cache, v_cache, block_table, seq_lens, seq_ids, o)):
         raise ValueError("all tensors must be on the same CUDA device")
     if k_cache.shape != v_cache.shape or k_cache.dim() != 5:
         raise ValueError("k_cache/v_cache must be [num_blocks, num_layers, num_kv_heads, block_size, head_dim]")
@@ -115,14 +148,17 @@ def paged_attention_raw(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
         raise ValueError("q, o, seq_lens and seq_ids disagree on the number of rows")
     if kernel is None:
         kernel = choose_kernel(num_q_heads, num_kv_heads, num_rows, max_len)
-    stream = stream or torch.cuda.current_stream(q.device)
+    if stream is not None:
+        stream_ptr = stream.cuda_stream
+    else:
+        stream_ptr = _raw_stream(q.get_device())
     if workspace is None:
-        workspace = attention_workspace(kernel, q.device, stream, num_rows, num_q_heads, num_kv_heads)
+        workspace = _last_workspace(kernel, q, stream, stream_ptr, num_rows, num_q_heads, num_kv_heads)
     rc = _entry(kernel)(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
             block_table.shape[0], block_table.shape[1], seq_lens.data_ptr(), seq_ids.data_ptr(),
             num_rows, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks, num_layers,
             cur_layer, float(softmax_scale), o.data_ptr(), workspace.data_ptr(), workspace.numel(),
-            stream.cuda_stream)
+            stream_ptr)
     _lib.check(rc, "paged_attention")
 
 
