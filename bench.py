@@ -915,6 +915,74 @@ def run_accept(args):
     print(json.dumps(line), flush=True)
 
 
+def run_prefill(args):
+    """Causal prefill attention of one Qwen3-8B layer (32 q / 8 kv heads, head
+    dim 128) over a packed batch of ragged prompts (seeded lengths U[64, 2048],
+    --requests prompts, default 16): the drop-in ``flash_attn_varlen_func``
+    (a one-CTA plan launch, then the tcgen05 prefill kernel) against the
+    reference's own function on the same GPU (``transformer_layer.py:7-32``:
+    ``cu_seqlens`` to the host, one ``scaled_dot_product_attention`` per
+    prompt).  q, k and v (about 170 MB) are larger than L2."""
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    from baseline import reference as R
+    nseq = args.requests or 16
+    g = torch.Generator().manual_seed(4242)
+    lens = torch.randint(64, 2049, (nseq,), generator=g).tolist()
+    heads, kv_heads, dim = 32, 8, 128
+    tokens = sum(lens)
+    gd = torch.Generator(device=dev).manual_seed(17)
+    q = torch.randn((tokens, heads, dim), generator=gd, device=dev).half()
+    k = torch.randn((tokens, kv_heads, dim), generator=gd, device=dev).half()
+    v = torch.randn((tokens, kv_heads, dim), generator=gd, device=dev).half()
+    cu = torch.tensor([0] + torch.cumsum(torch.tensor(lens), 0).tolist(), dtype=torch.int32, device=dev)
+    scale = dim ** -0.5
+
+    def ours():
+        return flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=scale, causal=True)
+
+    steps, warm = max(args.steps, 20), max(args.warmup, 3)
+    ms = _time_steps(ours, steps, warm)
+    # QK^T and PV over the causal triangle: 4 * heads * dim FLOPs per (query, key) pair
+    flops = sum(4 * heads * dim * n * (n + 1) / 2 for n in lens)
+    peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    tflops = flops / (ms * 1e-3) / 1e12
+    line = {"metric": "prefill attention ms per layer call (Qwen3-8B heads, packed ragged prompts)",
+            "value": round(ms, 4), "unit": "ms", "n_gpus": 1, "steps": steps, "warmup": warm,
+            "higher_is_better": False, "scaling": "none", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "prefill_8b", "prompts": nseq, "tokens": tokens, "max_len": max(lens),
+                       "heads": heads, "kv_heads": kv_heads},
+            "tokens_per_s": round(tokens / (ms * 1e-3)),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "flops_per_call": flops,
+                         "note": "whole call (plan launch included) against the fp16 causal-triangle FLOPs"},
+            "gpu_launches": 2 * steps}
+    if R.available():
+        ref_fn = R.swiftllm("worker.layers.transformer_layer").flash_attn_varlen_func
+
+        def ref():
+            return ref_fn(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=scale, causal=True)
+
+        for _ in range(warm):
+            ref()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            ref()
+        torch.cuda.synchronize()
+        ref_ms = (time.perf_counter() - t0) / steps * 1e3
+        err = (ours().float() - ref().float()).abs().max().item()
+        line["reference_gpu"] = {"impl": "the reference's flash_attn_varlen_func (per-prompt SDPA, host sync)",
+                                 "ms": round(ref_ms, 4), "speedup": round(ref_ms / ms, 3),
+                                 "max_abs_diff": err}
+    print(json.dumps(line), flush=True)
+
+
 def run_long_hostkv(args):
     world, rank, local = _dist()
     if rank != 0:
@@ -1083,6 +1151,7 @@ class _B200Ops:
                  ("rotary_embedding_inplace", "rotary_emb"), ("rmsnorm_inplace", "rmsnorm"))
         self.kernel_mods = {n: R.swiftllm(f"worker.kernels.{m}") for n, m in names}
         self.saved = {n: (getattr(self.layer_mod, n), getattr(self.kernel_mods[n], n)) for n, _ in names}
+        self.prefill = self.layer_mod.flash_attn_varlen_func
         self.copy_mod = sys.modules.get("nebulasd.kv.cuda_transfer")
         self.copy_backend = getattr(self.copy_mod, "CudaCopyBackend", None)
 
@@ -1095,6 +1164,7 @@ class _B200Ops:
         for n, (layer_fn, mod_fn) in self.saved.items():
             setattr(self.layer_mod, n, layer_fn)
             setattr(self.kernel_mods[n], n, mod_fn)
+        self.layer_mod.flash_attn_varlen_func = self.prefill
         if self.copy_mod is not None:
             self.copy_mod.CudaCopyBackend = self.copy_backend
         return False
@@ -1215,6 +1285,8 @@ def main():
         run_long_hostkv(args)
     elif args.workload == "greedy_accept_8b":
         run_accept(args)
+    elif args.workload == "prefill_8b":
+        run_prefill(args)
     elif args.workload == "fused_store_0p6b":
         run_fused(args)
     elif args.workload == "hostkv_copy":

@@ -156,7 +156,8 @@ int neb_paged_attention_verify_long(const void* q, const void* k_cache, const vo
 /* Synchronises `stream`, then reads the error bits the attention kernels
  * recorded in `workspace` (bit 0: block index out of range, bit 1: seq_id out
  * of range, bit 2: sequence longer than max_blocks_per_seq, bit 3: a bounded
- * wait gave up) and clears them.  After bit 3 it also clears the workspace's
+ * wait gave up, bit 4: invalid accept rows, bit 5: invalid prefill
+ * cu_seqlens) and clears them.  After bit 3 it also clears the workspace's
  * split-K arrival counters (the call that gave up left some of them counted),
  * so call it before reusing a workspace whose last call may have failed. */
 int neb_workspace_status(void* workspace, uint32_t* error_bits, void* stream);
@@ -191,6 +192,33 @@ int neb_greedy_accept(const void* logits, int64_t row_stride, int32_t vocab, int
                       const int32_t* remaining, const int32_t* stop_tokens, int32_t num_stop, int32_t max_out,
                       int32_t* argmax_out, int32_t* out_tokens, int32_t* out_count, int32_t* out_accepted,
                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ prefill attention
+ * Causal attention within each sequence of a packed prefill batch.  Replaces
+ * flash_attn_varlen_func (swiftLLM/swiftllm/worker/layers/transformer_layer.py:7-32,
+ * called at :154-164 with q and k covering the same sequences, causal=True),
+ * without its copy of cu_seqlens to the host.
+ *
+ * q            fp16 [total_tokens][num_q_heads][128], q_stride elements between tokens
+ * k, v         fp16 [total_tokens][num_kv_heads][128], k_stride / v_stride likewise
+ * cu_seqlens   int32 [num_seqs + 1] on the device: sequence s is tokens
+ *              cu_seqlens[s] .. cu_seqlens[s+1]-1 (cu_seqlens[0] = 0,
+ *              cu_seqlens[num_seqs] = total_tokens)
+ * max_seqlen   an upper bound of the sequence lengths (the reference's max_seqlen_q)
+ * o            fp16 [total_tokens][num_q_heads][128], o_stride elements between tokens
+ * q/kv head ratios 1, 2, 4, 8 and 16; head_dim 128; strides multiples of 8
+ * elements; every pointer 16-byte aligned.  The workspace
+ * (neb_prefill_attention_workspace_bytes) is zero-filled once; calls sharing
+ * it must be ordered on one stream.  A cu_seqlens that is not a split of the
+ * tokens, or a sequence longer than max_seqlen, is recorded as error bit 5
+ * (read with neb_workspace_status) and its sequences are left out. */
+size_t neb_prefill_attention_workspace_bytes(int64_t total_tokens, int32_t num_seqs, int32_t num_q_heads,
+                                             int32_t num_kv_heads);
+int neb_prefill_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride, const void* v,
+                          int64_t v_stride, const int32_t* cu_seqlens, int32_t num_seqs, int64_t total_tokens,
+                          int32_t max_seqlen, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          float softmax_scale, void* o, int64_t o_stride, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------ QK-norm, RoPE and KV store
  * Token layout of one forward (the reference's): prefill tokens first

@@ -6,6 +6,7 @@ Ops (``nebulasd_b200.kernels``), with the reference's names and signatures:
   * ``rotary_embedding_inplace`` RoPE
   * ``rmsnorm_inplace``          RMSNorm (Qwen3 QK-norm)
   * ``qk_norm_rope_store``       the last three fused into one launch
+  * ``flash_attn_varlen_func``   causal prefill attention (verify kernel, no host sync)
 HostKV (``nebulasd_b200.hostkv``): ``NativeCopyBackend`` for restore/writeback,
 ``migrate_blocks`` for same-role peer migration.
 
@@ -49,6 +50,10 @@ def install() -> None:
             for n in names:
                 if hasattr(layer, n):
                     setattr(layer, n, getattr(kernels, n))
+        # The prefill attention the layer module defines itself
+        # (transformer_layer.py:7-32): a per-sequence loop with a host sync.
+        if hasattr(layer, "flash_attn_varlen_func"):
+            layer.flash_attn_varlen_func = kernels.flash_attn_varlen_func
     kv = sys.modules.get("nebulasd.kv.cuda_transfer")
     if kv is not None:
         from .hostkv import NativeCopyBackend

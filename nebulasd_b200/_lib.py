@@ -48,6 +48,9 @@ SIGNATURES = {
     "neb_greedy_accept_workspace_bytes": ([_i32], _sz),
     "neb_greedy_accept": ([_vp, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
                            _sz, _vp], ctypes.c_int),
+    "neb_prefill_attention_workspace_bytes": ([_i64, _i32, _i32, _i32], _sz),
+    "neb_prefill_attention": ([_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i32, _i64, _i32, _i32, _i32, _i32, ctypes.c_float,
+                               _vp, _i64, _vp, _sz, _vp], ctypes.c_int),
 }
 
 for _name, (_args, _res) in SIGNATURES.items():
@@ -55,6 +58,7 @@ for _name, (_args, _res) in SIGNATURES.items():
     _fn.argtypes = _args
     _fn.restype = _res
 
+NEB_ERR_INVALID, NEB_ERR_UNSUPPORTED, NEB_ERR_CUDA, NEB_ERR_WORKSPACE, NEB_ERR_DEVICE = 1, 2, 3, 4, 5
 NEB_ATTN_DECODE = 0
 NEB_ATTN_VERIFY = 1
 NEB_ATTN_VERIFY_LONG = 2

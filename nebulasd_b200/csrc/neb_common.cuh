@@ -43,6 +43,7 @@ enum DeviceError : uint32_t {
   kErrTooManyBlocks = 1u << 2,  // sequence needs more than max_blocks_per_seq blocks
   kErrTimeout = 1u << 3,      // a bounded wait gave up
   kErrInvalidRows = 1u << 4,  // greedy accept: a request's rows or output limit are invalid
+  kErrBadSeqlens = 1u << 5,   // prefill: cu_seqlens not a valid split of the tokens (or past max_seqlen)
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

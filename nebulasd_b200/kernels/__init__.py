@@ -10,3 +10,4 @@ from .kvcache_mgmt import store_kvcache  # noqa: F401
 from .rotary_emb import rotary_embedding_inplace  # noqa: F401
 from .rmsnorm import rmsnorm_inplace  # noqa: F401
 from .fused import qk_norm_rope_store  # noqa: F401
+from .prefill import flash_attn_varlen_func  # noqa: F401

@@ -19,6 +19,7 @@ def test_header_declares_the_hot_path():
     for must in ("neb_paged_attention_decode", "neb_paged_attention_verify", "neb_store_kvcache",
                  "neb_qk_norm_rope_store", "neb_rotary_inplace", "neb_rmsnorm_inplace", "neb_hostkv_copy",
                  "neb_greedy_accept", "neb_greedy_accept_workspace_bytes",
+                 "neb_prefill_attention", "neb_prefill_attention_workspace_bytes",
                  "neb_kv_peer_copy"):
         assert must in names
 
@@ -152,6 +153,32 @@ def test_greedy_accept_rejects_bad_arguments_on_the_host():
     assert lib.neb_greedy_accept(*ok_empty) == 0  # nothing to do
     bad = list(args); bad[16] = 8                 # workspace too small
     assert lib.neb_greedy_accept(*bad) != 0
+
+
+def test_prefill_rejects_bad_arguments_on_the_host():
+    """Argument checks of the prefill entry run before any device work (no GPU needed)."""
+    from nebulasd_b200 import _lib
+    lib = _lib.lib
+    ws = lib.neb_prefill_attention_workspace_bytes(1000, 4, 32, 8)
+    # units of 32 tokens x 8 kv heads: at most ceil(1000 / 32) + 4 per head, 16 bytes each
+    assert ws >= 8 * (32 + 4) * 16
+    assert lib.neb_prefill_attention_workspace_bytes(1000, 4, 30, 8) == 0  # heads not a multiple
+    p = 1 << 20
+    args = [p, 32 * 128, p, 8 * 128, p, 8 * 128, p, 4, 1000, 512, 32, 8, 128, 0.088, p, 32 * 128, p, ws, None]
+    empty = list(args); empty[7] = 0
+    assert lib.neb_prefill_attention(*empty) == 0               # no sequences: nothing to do
+    bad = list(args); bad[10] = 24                              # q/kv head ratio 3: not this kernel's
+    assert lib.neb_prefill_attention(*bad) == _lib.NEB_ERR_UNSUPPORTED
+    bad = list(args); bad[12] = 64                              # head_dim 64
+    assert lib.neb_prefill_attention(*bad) == _lib.NEB_ERR_UNSUPPORTED
+    bad = list(args); bad[1] = 16 * 128                         # q token stride shorter than its heads
+    assert lib.neb_prefill_attention(*bad) != 0
+    bad = list(args); bad[2] = p + 8                            # k not 16-byte aligned
+    assert lib.neb_prefill_attention(*bad) != 0
+    bad = list(args); bad[17] = ws - 16                         # workspace too small
+    assert lib.neb_prefill_attention(*bad) != 0
+    bad = list(args); bad[9] = -1                               # negative max_seqlen
+    assert lib.neb_prefill_attention(*bad) != 0
 
 
 def test_accept_batch_validates_like_the_reference():

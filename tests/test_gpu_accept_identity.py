@@ -93,6 +93,7 @@ class _Kernels:
                             (("paged_attention", "paged_attn"), ("store_kvcache", "kvcache_mgmt"),
                              ("rotary_embedding_inplace", "rotary_emb"), ("rmsnorm_inplace", "rmsnorm"))}
         self.saved = {n: (getattr(self.layer_mod, n), getattr(self.kernel_mods[n], n)) for n in _PATCHED}
+        self.prefill = self.layer_mod.flash_attn_varlen_func
         self.copy_mod = sys.modules.get("nebulasd.kv.cuda_transfer")
         self.copy_backend = getattr(self.copy_mod, "CudaCopyBackend", None)
 
@@ -106,6 +107,7 @@ class _Kernels:
         for n, (layer_fn, mod_fn) in self.saved.items():
             setattr(self.layer_mod, n, layer_fn)
             setattr(self.kernel_mods[n], n, mod_fn)
+        self.layer_mod.flash_attn_varlen_func = self.prefill
         if self.copy_mod is not None:
             self.copy_mod.CudaCopyBackend = self.copy_backend
         return False

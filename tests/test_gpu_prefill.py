@@ -1,0 +1,111 @@
+"""GPU: causal prefill attention over packed variable-length sequences (the
+drop-in for ``flash_attn_varlen_func``, ``transformer_layer.py:7-32``) against
+an fp32 per-sequence restatement and against the reference's own function.
+Tolerance: |ours - fp32| <= 2e-3 + 1e-2 |fp32| (fp16 P and output)."""
+import pytest
+import torch
+
+from baseline import reference as R
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _case(lens, heads, kv_heads, seed, dev, q_pad=0):
+    g = torch.Generator().manual_seed(seed)
+    t = sum(lens)
+    qbig = torch.randn((t, heads + q_pad, 128), generator=g).half().to(dev)
+    q = qbig[:, :heads]  # token stride (heads + q_pad) * 128 when padded
+    k = torch.randn((t, kv_heads, 128), generator=g).half().to(dev)
+    v = torch.randn((t, kv_heads, 128), generator=g).half().to(dev)
+    cu = torch.tensor([0] + torch.cumsum(torch.tensor(lens), 0).tolist(), dtype=torch.int32, device=dev)
+    return q, k, v, cu
+
+
+def _fp32(q, k, v, cu, scale):
+    out = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+    c = cu.tolist()
+    rep = q.shape[1] // k.shape[1]
+    for s, e in zip(c[:-1], c[1:]):
+        if e == s:
+            continue
+        qi = q[s:e].float().transpose(0, 1)
+        ki = k[s:e].float().transpose(0, 1).repeat_interleave(rep, 0)
+        vi = v[s:e].float().transpose(0, 1).repeat_interleave(rep, 0)
+        att = (qi @ ki.transpose(1, 2)) * scale
+        n = e - s
+        att = att.masked_fill(torch.triu(torch.ones(n, n, dtype=torch.bool, device=q.device), 1), float("-inf"))
+        out[s:e] = (att.softmax(-1) @ vi).transpose(0, 1)
+    return out
+
+
+@pytest.mark.parametrize("lens,heads,kv_heads", [
+    ([1, 15, 16, 17, 100, 513], 32, 8),        # Qwen3-8B heads (ratio 4), ragged incl. block edges
+    ([127, 128, 129, 255, 256, 257], 32, 8),   # key-tile edges
+    ([300, 7, 1024, 64], 16, 8),               # Qwen3-0.6B heads (ratio 2)
+    ([2500, 300, 0, 41], 32, 8),               # an empty sequence; more rows than one verify call takes
+    ([5, 700], 8, 8),                          # ratio 1
+    ([333, 64, 9], 64, 8),                     # ratio 8
+    ([200, 31], 32, 2),                        # ratio 16
+    ([77, 400], 24, 8),                        # ratio 3: the verify-kernel path
+])
+def test_matches_fp32_reference(lens, heads, kv_heads, cuda):
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    q, k, v, cu = _case(lens, heads, kv_heads, sum(lens) + heads, cuda)
+    scale = 128 ** -0.5
+    out = flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=scale, causal=True)
+    torch.testing.assert_close(out.float(), _fp32(q, k, v, cu, scale), atol=ATOL, rtol=RTOL)
+
+
+def test_many_short_prompts_and_a_strided_q(cuda):
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    g = torch.Generator().manual_seed(5)
+    lens = torch.randint(1, 60, (300,), generator=g).tolist() + [1500]
+    q, k, v, cu = _case(lens, 32, 8, 11, cuda, q_pad=8)
+    assert q.stride(0) == 40 * 128
+    scale = 0.1
+    out = flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=scale, causal=True)
+    torch.testing.assert_close(out.float(), _fp32(q, k, v, cu, scale), atol=ATOL, rtol=RTOL)
+
+
+def test_large_scores_move_the_running_max(cuda):
+    """Scores whose row max grows along the keys (rescaled O) and spans > 2^8 in exp2."""
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    lens = [1000, 600]
+    q, k, v, cu = _case(lens, 32, 8, 3, cuda)
+    ramp = torch.linspace(0.2, 3.0, sum(lens), device=cuda).half()[:, None, None]
+    k = (k * ramp).contiguous()
+    scale = 0.3
+    out = flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=scale, causal=True)
+    torch.testing.assert_close(out.float(), _fp32(q, k, v, cu, scale), atol=ATOL, rtol=RTOL)
+
+
+def test_invalid_cu_seqlens_is_reported(cuda):
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    from nebulasd_b200.kernels.prefill import workspace_errors
+    q, k, v, _ = _case([20], 32, 8, 1, cuda)
+    assert workspace_errors() == 0
+    # sequence 1 ends past the tokens, sequence 2 has a negative length: both left out
+    bad = torch.tensor([0, 10, 30, 20], dtype=torch.int32, device=cuda)
+    out = flash_attn_varlen_func(q, k, v, bad, bad, 20, 20)
+    assert workspace_errors() & (1 << 5)
+    # the valid sequence is still computed
+    ref = _fp32(q, k, v, torch.tensor([0, 10], dtype=torch.int32, device=cuda), 128 ** -0.5)
+    torch.testing.assert_close(out[:10].float(), ref[:10], atol=ATOL, rtol=RTOL)
+    longer = torch.tensor([0, 20], dtype=torch.int32, device=cuda)
+    flash_attn_varlen_func(q, k, v, longer, longer, 8, 8)  # max_seqlen below the real length
+    assert workspace_errors() & (1 << 5)
+    assert workspace_errors() == 0
+
+
+@pytest.mark.skipif(not R.available(), reason="reference not installed under baseline/_ref")
+def test_matches_the_reference_function(cuda):
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    ref_fn = R.swiftllm("worker.layers.transformer_layer").flash_attn_varlen_func
+    assert ref_fn.__module__.startswith("swiftllm."), "another test left install() in place"
+    lens = [129, 700, 33, 1000]
+    q, k, v, cu = _case(lens, 32, 8, 7, cuda)
+    scale = 128 ** -0.5
+    ours = flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=scale, causal=True)
+    theirs = ref_fn(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=scale, causal=True)
+    torch.testing.assert_close(ours.float(), theirs.float(), atol=4e-3, rtol=1e-2)
