@@ -27,13 +27,16 @@
 //                  of two TMEM S buffers, then O += P V of the previous tile
 //                  into one of two TMEM O buffers, so that the tensor core
 //                  computes the next S while the softmax works on this one.
-//       warps 2-5  softmax, one row per thread (TMEM lane quadrant warp % 4):
-//                  the row's 128 scores from TMEM, the mask of the last tile,
-//                  the running max (moved only when it grows by more than 8
-//                  in the exp2 domain, O then rescaled in TMEM), P = 2^(s - m)
-//                  as fp16 into the swizzled P tile in shared memory, and the
-//                  fp32 row sum of exactly those fp16 values.
-//       warps 6-9  epilogue: O / l of a finished unit as fp16 rows of the
+//                  P V takes P from TMEM (A operand) and V from shared memory;
+//                  the S buffer is reused once that P V has completed.
+//       warps 2-9  softmax, two warps per TMEM lane quadrant, one row and 64
+//                  columns per thread: the row's scores from TMEM, the mask of
+//                  the last tile, the running max (both halves' maxima
+//                  exchanged through shared memory; moved only when it grows
+//                  by more than 8 in the exp2 domain, O then rescaled in
+//                  TMEM), P = 2^(s - m) as fp16 pairs back into the S buffer,
+//                  and the fp32 row sum of exactly those fp16 values.
+//       warps 10-13 epilogue: O / l of a finished unit as fp16 rows of the
 //                  output while the other warps go on with the next unit.
 //
 // Every wait is bounded (about 2 s); on expiry the kernel records kErrTimeout
@@ -54,11 +57,12 @@ using namespace sm100;
 
 namespace prefill {
 
-constexpr int kThreads = 320;  // 10 warps: 0 loads, 1 MMA, 2-5 softmax, 6-9 epilogue
+constexpr int kThreads = 448;  // 14 warps: 0 loads, 1 MMA, 2-9 softmax, 10-13 epilogue
 constexpr int kLoadWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kSoftmaxWarp0 = 2;
-constexpr int kEpiWarp0 = 6;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kEpiWarp0 = kSoftmaxWarp0 + kSoftmaxWarps;
 constexpr int kRows = 128;     // MMA M: query rows of a unit
 constexpr int kKeys = 128;     // keys of a tile: the S tile's N
 constexpr uint32_t kTmemCols = 512;
@@ -71,9 +75,9 @@ constexpr uint32_t kTile = 2 * kHalf;        // Q of a unit, or K or V of a tile
 constexpr uint32_t kQOff = 0;                // two Q buffers
 constexpr uint32_t kKOff = kQOff + 2 * kTile;  // K ring, two slots
 constexpr uint32_t kVOff = kKOff + 2 * kTile;  // V ring, two slots
-constexpr uint32_t kPOff = kVOff + 2 * kTile;  // P: two 64-key atoms of 128 rows
-constexpr uint32_t kStatOff = kPOff + kTile;   // row sums of a finished unit: [2][128] float
-constexpr uint32_t kBarOff = kStatOff + 2 * kRows * 4;
+constexpr uint32_t kXOff = kVOff + 2 * kTile;  // partial row maxima: [2 tiles][2 halves][128] float
+constexpr uint32_t kStatOff = kXOff + 2 * 2 * kRows * 4;  // partial row sums: [2 units][2 halves][128]
+constexpr uint32_t kBarOff = kStatOff + 2 * 2 * kRows * 4;
 constexpr uint32_t kSmemBytes = kBarOff + 512 + 1024;  // + alignment pad
 static_assert(kSmemBytes <= 232448, "fits the 227 KB a CTA may use");
 
@@ -83,6 +87,7 @@ struct Shared {
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full, pv_done;
+  uint64_t xmax[4][2];  // per lane quadrant and tile parity: both halves' maxima written
   uint64_t o_full[2], o_empty[2];
   uint64_t st_full[2], st_empty[2];
   uint64_t mma_final;
@@ -224,7 +229,10 @@ struct PvTile {
   int G, k, j, nt;
 };
 
-__device__ __forceinline__ bool issue_pv(Shared* sh, const Args& a, uint32_t tmem, uint32_t v_base, uint32_t p_base,
+// O += P V of tile t.G: P (fp16, 64 columns) in the first half of the tile's
+// TMEM S buffer, V from shared memory.  The S buffer is free again once this
+// P V has completed.
+__device__ __forceinline__ bool issue_pv(Shared* sh, const Args& a, uint32_t tmem, uint32_t v_base,
                                          const PvTile& t) {
   const int ob = t.k & 1, slot = t.G & 1;
   if (!wt(sh, a.hdr, &sh->p_full, t.G & 1) || !wt(sh, a.hdr, &sh->v_full[slot], (t.G >> 1) & 1) ||
@@ -232,14 +240,13 @@ __device__ __forceinline__ bool issue_pv(Shared* sh, const Args& a, uint32_t tme
     return false;
   tc_fence_after();
   const uint32_t idesc = idesc_f16_f32(kRows, 128, false, true);
-  const uint64_t pa0 = smem_desc_sw128(p_base, 16, 1024);
   const uint64_t vb0 = smem_desc_sw128(v_base + slot * kTile, kHalf, 1024);
-  const uint32_t ocol = tmem + kOCol + 128u * ob;
+  const uint32_t ocol = tmem + kOCol + 128u * ob, pcol = tmem + 128u * slot;
 #pragma unroll
   for (int kb = 0; kb < kKeys / 16; ++kb)
-    mma_f16(ocol, pa0 + (((kb >> 2) * kHalf + (kb & 3) * 32) >> 4), vb0 + ((kb * 2048) >> 4), idesc,
-            (t.j > 0 || kb > 0) ? 1u : 0u);
+    mma_f16_ta(ocol, pcol + 8u * kb, vb0 + ((kb * 2048) >> 4), idesc, (t.j > 0 || kb > 0) ? 1u : 0u);
   mma_commit(&sh->v_empty[slot]);
+  mma_commit(&sh->s_empty[slot]);
   mma_commit(&sh->pv_done);
   if (t.j == t.nt - 1) mma_commit(&sh->o_full[ob]);
   return true;
@@ -248,7 +255,7 @@ __device__ __forceinline__ bool issue_pv(Shared* sh, const Args& a, uint32_t tme
 __device__ __noinline__ void mma_role(Shared* sh, const Args& a, uint8_t* smem) {
   const uint32_t tmem = sh->tmem_base;
   const uint32_t q_base = smem_u32(smem + kQOff), k_base = smem_u32(smem + kKOff);
-  const uint32_t v_base = smem_u32(smem + kVOff), p_base = smem_u32(smem + kPOff);
+  const uint32_t v_base = smem_u32(smem + kVOff);
   const uint32_t idesc_s = idesc_f16_f32(kRows, kKeys, false, false);
   Cursor cur;
   cur.init(a.units, sh->num_units);
@@ -276,7 +283,7 @@ __device__ __noinline__ void mma_role(Shared* sh, const Args& a, uint8_t* smem) 
       mma_commit(&sh->s_full[slot]);
       mma_commit(&sh->k_empty[slot]);
       if (j == nt - 1) mma_commit(&sh->q_empty[qb]);
-      if (have_prev && !issue_pv(sh, a, tmem, v_base, p_base, prev)) {
+      if (have_prev && !issue_pv(sh, a, tmem, v_base, prev)) {
         ok = false;
         break;
       }
@@ -284,36 +291,43 @@ __device__ __noinline__ void mma_role(Shared* sh, const Args& a, uint8_t* smem) 
       have_prev = true;
     }
   }
-  if (ok && have_prev) issue_pv(sh, a, tmem, v_base, p_base, prev);
+  if (ok && have_prev) issue_pv(sh, a, tmem, v_base, prev);
   // Every MMA issued has completed before the CTA frees its tensor memory.
   mma_commit(&sh->mma_final);
   mbar_wait(&sh->mma_final, 0, kWaitLimit);
 }
 
 // ---------------------------------------------------------------- softmax
-__device__ __noinline__ void rescale_o(uint32_t ocol, float alpha) {
+// Two warps per TMEM lane quadrant: warp w (quadrant w % 4, half h = (w - 2) / 4)
+// holds, per thread, one row (lane) and the 64 key columns 64 h .. 64 h + 63 of
+// it (32x32b loads).  The two halves of a row exchange their maxima through
+// shared memory and a per-quadrant mbarrier.  P goes back into the first 64
+// columns of the tile's S buffer as fp16 pairs (key 2c and 2c + 1 in column c),
+// the A operand of P V.
+
+// O columns 64 h .. 64 h + 63 of this thread's row times alpha, in TMEM.
+__device__ __noinline__ void rescale_o(uint32_t oaddr, float alpha) {
 #pragma unroll 1
-  for (int c = 0; c < 128; c += 16) {
+  for (int c = 0; c < 64; c += 16) {
     uint32_t r[16];
-    tmem_ld_32x32b_x16(ocol + c, r);
+    tmem_ld_32x32b_x16(oaddr + c, r);
     tmem_wait_ld();
 #pragma unroll
     for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-    tmem_st_32x32b_x16(ocol + c, r);
+    tmem_st_32x32b_x16(oaddr + c, r);
   }
   tmem_wait_st();
 }
 
 __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* smem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int quad = warp & 3, row = 32 * quad + lane;
-  const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
-  const uint32_t tmem = sh->tmem_base + lane_addr;
+  const int quad = warp & 3, half = (warp - kSoftmaxWarp0) >> 2;
+  const int row = 32 * quad + lane;
+  const uint32_t tmem = sh->tmem_base + ((uint32_t)(32 * quad) << 16);
   const float sc = a.scale_log2;
+  float* xmax = reinterpret_cast<float*>(smem + kXOff);   // [tile parity][half][row]
+  float* stats = reinterpret_cast<float*>(smem + kStatOff);  // [unit parity][half][row]
   const int tok_in_unit = row / a.gqa;
-  uint8_t* prow = smem + kPOff + row * 128;
-  const int sw = row & 7;
-  float* stats = reinterpret_cast<float*>(smem + kStatOff);
   Cursor cur;
   cur.init(a.units, sh->num_units);
   Unit u;
@@ -321,8 +335,8 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
   bool ok = true;
   for (int k = 0; ok && cur.next(u); ++k) {
     const int ob = k & 1, nt = tiles_of(u, a.tq);
-    const int t = u.qs + tok_in_unit;            // this row's token within its sequence
-    const int vis = min(t + 1, u.n);             // keys it sees (invalid rows: all n)
+    // Keys this row sees: its token + 1 (rows past the sequence: all of it).
+    const int vis = min(u.qs + tok_in_unit + 1, u.n);
     float m = neg_inf(), l = 0.f;
     for (int j = 0; j < nt; ++j, ++G) {
       const int sb = G & 1;
@@ -331,67 +345,67 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
         break;
       }
       tc_fence_after();
-      uint32_t s[128];
+      const uint32_t scol = tmem + 128u * sb;
+      uint32_t s[64];
 #pragma unroll
-      for (int c = 0; c < 128; c += 16) tmem_ld_32x32b_x16(tmem + 128u * sb + c, s + c);
+      for (int c = 0; c < 64; c += 16) tmem_ld_32x32b_x16(scol + 64 * half + c, s + c);
       tmem_wait_ld();
-      tc_fence_before();
-      warp_arrive(&sh->s_empty[sb]);
       if (j == nt - 1) {
-        const int lim = vis - j * kKeys;  // >= 1
+        const int lim = vis - j * kKeys - 64 * half;
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
+        for (int c = 0; c < 64; ++c)
           if (c >= lim) s[c] = __float_as_uint(neg_inf());
       }
-      float mx4[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
+      float t4[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
 #pragma unroll
-      for (int c = 0; c < 128; c += 4) {
+      for (int c = 0; c < 64; c += 4)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) mx4[e] = fmaxf(mx4[e], __uint_as_float(s[c + e]));
-      }
-      const float mxs = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc;
-      float alpha = 1.f;
-      if (j == 0) {
-        m = mxs;
-      } else if (mxs > m + 8.f) {
-        alpha = fast_exp2(m - mxs);
-        m = mxs;
-      }
-      // The P tile is free, and O complete up to the previous tile, once the
-      // previous P V has completed.
-      if (G > 0 && !wt_warp(sh, a.hdr, &sh->pv_done, (G - 1) & 1)) {
+        for (int e = 0; e < 4; ++e) t4[e] = fmaxf(t4[e], __uint_as_float(s[c + e]));
+      float mx = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
+      xmax[(sb * 2 + half) * kRows + row] = mx;
+      warp_arrive(&sh->xmax[quad][sb]);
+      if (!wt_warp(sh, a.hdr, &sh->xmax[quad][sb], (G >> 1) & 1)) {
         ok = false;
         break;
       }
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
-        tc_fence_after();
-        rescale_o(tmem + kOCol + 128u * ob, alpha);
+      mx = fmaxf(mx, xmax[(sb * 2 + (half ^ 1)) * kRows + row]);
+      const float mxs = mx * sc;
+      float alpha = 1.f;
+      if (j == 0) {
+        m = mxs;
+      } else if (mxs > m + 8.f) {  // lazy: the max moves only when it grew by more than 2^8
+        alpha = fast_exp2(m - mxs);
+        m = mxs;
       }
-      l *= alpha;
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        // O is complete up to the previous tile once its P V has completed.
+        if (!wt_warp(sh, a.hdr, &sh->pv_done, (G - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        rescale_o(tmem + kOCol + 128u * ob + 64 * half, alpha);
+      }
       const float negm = -m;
-      uint32_t pk[64];
+      uint32_t pk[32];
+      float acc[2] = {0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 64; ++i)
+      for (int i = 0; i < 32; ++i) {
         pk[i] = ex2_f16x2(f2_to_h2(fmaf(__uint_as_float(s[2 * i]), sc, negm),
                                    fmaf(__uint_as_float(s[2 * i + 1]), sc, negm)));
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
         const float2 f = h2_to_f2(pk[i]);
-        acc[i & 3] += f.x + f.y;
+        acc[i & 1] += f.x + f.y;
       }
-      l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
-#pragma unroll
-      for (int g = 0; g < 16; ++g)
-        st_shared_v4(smem_u32(prow + (g >> 3) * kHalf + (((g & 7) ^ sw) << 4)), pk[4 * g], pk[4 * g + 1],
-                     pk[4 * g + 2], pk[4 * g + 3]);
-      fence_proxy_async_smem();
+      l = l * alpha + (acc[0] + acc[1]);
+      tmem_st_32x32b_x16(scol + 32 * half, pk);
+      tmem_st_32x32b_x16(scol + 32 * half + 16, pk + 16);
+      tmem_wait_st();
       tc_fence_before();
       warp_arrive(&sh->p_full);
     }
     if (!ok) break;
     if (!wt_warp(sh, a.hdr, &sh->st_empty[ob], ((k >> 1) & 1) ^ 1)) break;
-    stats[ob * kRows + row] = l;
+    stats[(ob * 2 + half) * kRows + row] = l;
     warp_arrive(&sh->st_full[ob]);
   }
 }
@@ -411,7 +425,7 @@ __device__ __noinline__ void epilogue_role(Shared* sh, const Args& a, uint8_t* s
     if (!wt_warp(sh, a.hdr, &sh->st_full[ob], (k >> 1) & 1) || !wt_warp(sh, a.hdr, &sh->o_full[ob], (k >> 1) & 1))
       break;
     tc_fence_after();
-    const float inv = 1.f / stats[ob * kRows + row];
+    const float inv = 1.f / (stats[(ob * 2) * kRows + row] + stats[(ob * 2 + 1) * kRows + row]);
     const int t = u.qs + tok_in_unit;
     const bool valid = t < u.n;
     __half* dst = a.o + (long long)(u.ts + t) * a.o_stride + (long long)(u.h * a.gqa + head_in_unit) * kHeadDim;
@@ -453,14 +467,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sh->v_full[i], 1);
       mbar_init(&sh->v_empty[i], 1);
       mbar_init(&sh->s_full[i], 1);
-      mbar_init(&sh->s_empty[i], 4);
+      mbar_init(&sh->s_empty[i], 1);
       mbar_init(&sh->o_full[i], 1);
       mbar_init(&sh->o_empty[i], 4);
-      mbar_init(&sh->st_full[i], 4);
+      mbar_init(&sh->st_full[i], kSoftmaxWarps);
       mbar_init(&sh->st_empty[i], 4);
     }
-    mbar_init(&sh->p_full, 4);
+    mbar_init(&sh->p_full, kSoftmaxWarps);
     mbar_init(&sh->pv_done, 1);
+    for (int q = 0; q < 4; ++q)
+      for (int i = 0; i < 2; ++i) mbar_init(&sh->xmax[q][i], 2);
     mbar_init(&sh->mma_final, 1);
     sh->abort_flag = 0;
     fence_mbar_init();
