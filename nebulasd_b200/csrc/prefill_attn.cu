@@ -29,13 +29,13 @@
 //                  computes the next S while the softmax works on this one.
 //                  P V takes P from TMEM (A operand) and V from shared memory;
 //                  the S buffer is reused once that P V has completed.
-//       warps 2-9  softmax, two warps per TMEM lane quadrant, one row and 64
-//                  columns per thread: the row's scores from TMEM, the mask of
-//                  the last tile, the running max (both halves' maxima
-//                  exchanged through shared memory; moved only when it grows
-//                  by more than 8 in the exp2 domain, O then rescaled in
-//                  TMEM), P = 2^(s - m) as fp16 pairs back into the S buffer,
-//                  and the fp32 row sum of exactly those fp16 values.
+//       warps 2-9  softmax, two warps per TMEM lane quadrant, 16 rows each
+//                  (two rows x 32 columns per thread): the rows' scores from
+//                  TMEM, the mask of the last tile, the running max (moved
+//                  only when it grows by more than 8 in the exp2 domain, O
+//                  then rescaled in TMEM), P = 2^(s - m) as fp16 pairs back
+//                  into the S buffer, and the fp32 row sum of exactly those
+//                  fp16 values.
 //       warps 10-13 epilogue: O / l of a finished unit as fp16 rows of the
 //                  output while the other warps go on with the next unit.
 //
@@ -75,9 +75,8 @@ constexpr uint32_t kTile = 2 * kHalf;        // Q of a unit, or K or V of a tile
 constexpr uint32_t kQOff = 0;                // two Q buffers
 constexpr uint32_t kKOff = kQOff + 2 * kTile;  // K ring, two slots
 constexpr uint32_t kVOff = kKOff + 2 * kTile;  // V ring, two slots
-constexpr uint32_t kXOff = kVOff + 2 * kTile;  // partial row maxima: [2 tiles][2 halves][128] float
-constexpr uint32_t kStatOff = kXOff + 2 * 2 * kRows * 4;  // partial row sums: [2 units][2 halves][128]
-constexpr uint32_t kBarOff = kStatOff + 2 * 2 * kRows * 4;
+constexpr uint32_t kStatOff = kVOff + 2 * kTile;  // row sums of a finished unit: [2 units][128] float
+constexpr uint32_t kBarOff = kStatOff + 2 * kRows * 4;
 constexpr uint32_t kSmemBytes = kBarOff + 512 + 1024;  // + alignment pad
 static_assert(kSmemBytes <= 232448, "fits the 227 KB a CTA may use");
 
@@ -87,7 +86,6 @@ struct Shared {
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full, pv_done;
-  uint64_t xmax[4][2];  // per lane quadrant and tile parity: both halves' maxima written
   uint64_t o_full[2], o_empty[2];
   uint64_t st_full[2], st_empty[2];
   uint64_t mma_final;
@@ -298,23 +296,31 @@ __device__ __noinline__ void mma_role(Shared* sh, const Args& a, uint8_t* smem) 
 }
 
 // ---------------------------------------------------------------- softmax
-// Two warps per TMEM lane quadrant: warp w (quadrant w % 4, half h = (w - 2) / 4)
-// holds, per thread, one row (lane) and the 64 key columns 64 h .. 64 h + 63 of
-// it (32x32b loads).  The two halves of a row exchange their maxima through
-// shared memory and a per-quadrant mbarrier.  P goes back into the first 64
-// columns of the tile's S buffer as fp16 pairs (key 2c and 2c + 1 in column c),
-// the A operand of P V.
+// Two warps per TMEM lane quadrant: warp w (quadrant w % 4, h = (w - 2) / 4)
+// owns the 16 lanes (rows) 32 (w % 4) + 16 h .. + 15.  In 16x256b loads each
+// thread holds 32 columns of two rows, a = base + lane / 4 and b = a + 8:
+// element (x, e) of column group R (0..15) is s[4R + 2x + e], at column
+// 8R + 2 (lane % 4) + e, so a row's max and sum take two shuffles within its
+// four threads and no other warp is waited for.  P goes back into the first
+// 64 columns of the tile's S buffer as fp16 pairs (keys 2c and 2c + 1 in
+// column c): with the 16x128b store, register 2R (row a) and 2R + 1 (row b)
+// land in column 4R + lane % 4, the pair of keys 8R + 2 (lane % 4) + {0, 1}.
 
-// O columns 64 h .. 64 h + 63 of this thread's row times alpha, in TMEM.
-__device__ __noinline__ void rescale_o(uint32_t oaddr, float alpha) {
+// O of this warp's rows times (alpha_a, alpha_b), in TMEM.
+__device__ __noinline__ void rescale_o(uint32_t oaddr, float alpha_a, float alpha_b) {
 #pragma unroll 1
-  for (int c = 0; c < 64; c += 16) {
-    uint32_t r[16];
-    tmem_ld_32x32b_x16(oaddr + c, r);
+  for (int half = 0; half < 2; ++half) {
+    uint32_t r[32];
+    tmem_ld_16x256b_x8(oaddr + half * 64, r);
     tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-    tmem_st_32x32b_x16(oaddr + c, r);
+    for (int i = 0; i < 8; ++i) {
+      r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) * alpha_a);
+      r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) * alpha_a);
+      r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) * alpha_b);
+      r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) * alpha_b);
+    }
+    tmem_st_16x256b_x8(oaddr + half * 64, r);
   }
   tmem_wait_st();
 }
@@ -322,12 +328,12 @@ __device__ __noinline__ void rescale_o(uint32_t oaddr, float alpha) {
 __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* smem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3, half = (warp - kSoftmaxWarp0) >> 2;
-  const int row = 32 * quad + lane;
-  const uint32_t tmem = sh->tmem_base + ((uint32_t)(32 * quad) << 16);
+  const int base = 32 * quad + 16 * half;  // first TMEM lane (row) of this warp
+  const int q4 = lane & 3;
+  const int row[2] = {base + (lane >> 2), base + (lane >> 2) + 8};
+  const uint32_t tmem = sh->tmem_base + ((uint32_t)base << 16);
   const float sc = a.scale_log2;
-  float* xmax = reinterpret_cast<float*>(smem + kXOff);   // [tile parity][half][row]
-  float* stats = reinterpret_cast<float*>(smem + kStatOff);  // [unit parity][half][row]
-  const int tok_in_unit = row / a.gqa;
+  float* stats = reinterpret_cast<float*>(smem + kStatOff);  // [unit parity][row]
   Cursor cur;
   cur.init(a.units, sh->num_units);
   Unit u;
@@ -335,9 +341,10 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
   bool ok = true;
   for (int k = 0; ok && cur.next(u); ++k) {
     const int ob = k & 1, nt = tiles_of(u, a.tq);
-    // Keys this row sees: its token + 1 (rows past the sequence: all of it).
-    const int vis = min(u.qs + tok_in_unit + 1, u.n);
-    float m = neg_inf(), l = 0.f;
+    int vis[2];  // keys each row sees: its token + 1 (rows past the sequence: all of it)
+#pragma unroll
+    for (int x = 0; x < 2; ++x) vis[x] = min(u.qs + row[x] / a.gqa + 1, u.n);
+    float m[2] = {neg_inf(), neg_inf()}, l[2] = {0.f, 0.f};
     for (int j = 0; j < nt; ++j, ++G) {
       const int sb = G & 1;
       if (!wt_warp(sh, a.hdr, &sh->s_full[sb], (G >> 1) & 1)) {
@@ -347,65 +354,79 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
       tc_fence_after();
       const uint32_t scol = tmem + 128u * sb;
       uint32_t s[64];
-#pragma unroll
-      for (int c = 0; c < 64; c += 16) tmem_ld_32x32b_x16(scol + 64 * half + c, s + c);
+      tmem_ld_16x256b_x8(scol, *reinterpret_cast<uint32_t(*)[32]>(s));
+      tmem_ld_16x256b_x8(scol + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
       tmem_wait_ld();
       if (j == nt - 1) {
-        const int lim = vis - j * kKeys - 64 * half;
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c >= lim) s[c] = __float_as_uint(neg_inf());
-      }
-      float t4[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
+        for (int x = 0; x < 2; ++x) {
+          const int lim = vis[x] - j * kKeys - 2 * q4;
 #pragma unroll
-      for (int c = 0; c < 64; c += 4)
+          for (int R = 0; R < 16; ++R)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) t4[e] = fmaxf(t4[e], __uint_as_float(s[c + e]));
-      float mx = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
-      xmax[(sb * 2 + half) * kRows + row] = mx;
-      warp_arrive(&sh->xmax[quad][sb]);
-      if (!wt_warp(sh, a.hdr, &sh->xmax[quad][sb], (G >> 1) & 1)) {
-        ok = false;
-        break;
+            for (int e = 0; e < 2; ++e)
+              if (8 * R + e >= lim) s[4 * R + 2 * x + e] = __float_as_uint(neg_inf());
+        }
       }
-      mx = fmaxf(mx, xmax[(sb * 2 + (half ^ 1)) * kRows + row]);
-      const float mxs = mx * sc;
-      float alpha = 1.f;
-      if (j == 0) {
-        m = mxs;
-      } else if (mxs > m + 8.f) {  // lazy: the max moves only when it grew by more than 2^8
-        alpha = fast_exp2(m - mxs);
-        m = mxs;
+      float alpha[2];
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        float t[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
+#pragma unroll
+        for (int R = 0; R < 16; ++R)
+          t[R & 3] = fmaxf(t[R & 3], fmaxf(__uint_as_float(s[4 * R + 2 * x]), __uint_as_float(s[4 * R + 2 * x + 1])));
+        float mx = fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mxs = mx * sc;
+        alpha[x] = 1.f;
+        if (j == 0) {
+          m[x] = mxs;
+        } else if (mxs > m[x] + 8.f) {  // lazy: the max moves only when it grew by more than 2^8
+          alpha[x] = fast_exp2(m[x] - mxs);
+          m[x] = mxs;
+        }
       }
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
         // O is complete up to the previous tile once its P V has completed.
         if (!wt_warp(sh, a.hdr, &sh->pv_done, (G - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        rescale_o(tmem + kOCol + 128u * ob + 64 * half, alpha);
+        rescale_o(tmem + kOCol + 128u * ob, alpha[0], alpha[1]);
       }
-      const float negm = -m;
-      uint32_t pk[32];
-      float acc[2] = {0.f, 0.f};
+      uint32_t pk[32];  // register 2R: row a, 2R + 1: row b (16x128b order)
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        pk[i] = ex2_f16x2(f2_to_h2(fmaf(__uint_as_float(s[2 * i]), sc, negm),
-                                   fmaf(__uint_as_float(s[2 * i + 1]), sc, negm)));
-        const float2 f = h2_to_f2(pk[i]);
-        acc[i & 1] += f.x + f.y;
+      for (int x = 0; x < 2; ++x) {
+        const float negm = -m[x];
+        float acc[2] = {0.f, 0.f};
+#pragma unroll
+        for (int R = 0; R < 16; ++R) {
+          const uint32_t h = ex2_f16x2(f2_to_h2(fmaf(__uint_as_float(s[4 * R + 2 * x]), sc, negm),
+                                                fmaf(__uint_as_float(s[4 * R + 2 * x + 1]), sc, negm)));
+          pk[2 * R + x] = h;
+          const float2 f = h2_to_f2(h);
+          acc[R & 1] += f.x + f.y;
+        }
+        l[x] = l[x] * alpha[x] + (acc[0] + acc[1]);
       }
-      l = l * alpha + (acc[0] + acc[1]);
-      tmem_st_32x32b_x16(scol + 32 * half, pk);
-      tmem_st_32x32b_x16(scol + 32 * half + 16, pk + 16);
+      tmem_st_16x128b_x16(scol, pk);
       tmem_wait_st();
       tc_fence_before();
       warp_arrive(&sh->p_full);
     }
     if (!ok) break;
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      l[x] += __shfl_xor_sync(0xffffffffu, l[x], 1);
+      l[x] += __shfl_xor_sync(0xffffffffu, l[x], 2);
+    }
     if (!wt_warp(sh, a.hdr, &sh->st_empty[ob], ((k >> 1) & 1) ^ 1)) break;
-    stats[(ob * 2 + half) * kRows + row] = l;
+    if (q4 == 0) {
+      stats[ob * kRows + row[0]] = l[0];
+      stats[ob * kRows + row[1]] = l[1];
+    }
     warp_arrive(&sh->st_full[ob]);
   }
 }
@@ -425,7 +446,7 @@ __device__ __noinline__ void epilogue_role(Shared* sh, const Args& a, uint8_t* s
     if (!wt_warp(sh, a.hdr, &sh->st_full[ob], (k >> 1) & 1) || !wt_warp(sh, a.hdr, &sh->o_full[ob], (k >> 1) & 1))
       break;
     tc_fence_after();
-    const float inv = 1.f / (stats[(ob * 2) * kRows + row] + stats[(ob * 2 + 1) * kRows + row]);
+    const float inv = 1.f / stats[ob * kRows + row];
     const int t = u.qs + tok_in_unit;
     const bool valid = t < u.n;
     __half* dst = a.o + (long long)(u.ts + t) * a.o_stride + (long long)(u.h * a.gqa + head_in_unit) * kHeadDim;
@@ -475,8 +496,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&sh->p_full, kSoftmaxWarps);
     mbar_init(&sh->pv_done, 1);
-    for (int q = 0; q < 4; ++q)
-      for (int i = 0; i < 2; ++i) mbar_init(&sh->xmax[q][i], 2);
     mbar_init(&sh->mma_final, 1);
     sh->abort_flag = 0;
     fence_mbar_init();
