@@ -23,12 +23,11 @@
 //       warp 0     loads: Q of a unit (two 3D boxes, 16 KB each) into one of
 //                  two Q buffers; K and V tiles of 128 keys (two boxes each)
 //                  into two-slot K and V rings (TMA, no multicast).
-//       warp 1     MMA issue (one thread): S = Q K^T (M=128, N=128) into one
-//                  of two TMEM S buffers, then O += P V of the previous tile
-//                  into one of two TMEM O buffers, so that the tensor core
-//                  computes the next S while the softmax works on this one.
-//                  P V takes P from TMEM (A operand) and V from shared memory;
-//                  the S buffer is reused once that P V has completed.
+//       warp 1     S issue (one thread): S = Q K^T (M=128, N=128) into one of
+//                  three TMEM S buffers, ahead of the softmax.
+//       warp 14    P V issue (one thread): O += P V into the TMEM O
+//                  accumulator, P from TMEM (A operand), V from shared
+//                  memory; an S buffer is reused once its P V has completed.
 //       warps 2-9  softmax, two warps per TMEM lane quadrant, 16 rows each
 //                  (two rows x 32 columns per thread): the rows' scores from
 //                  TMEM, the mask of the last tile, the running max (moved
@@ -36,8 +35,9 @@
 //                  then rescaled in TMEM), P = 2^(s - m) as fp16 pairs back
 //                  into the S buffer, and the fp32 row sum of exactly those
 //                  fp16 values.
-//       warps 10-13 epilogue: O / l of a finished unit as fp16 rows of the
-//                  output while the other warps go on with the next unit.
+//       warps 10-13 epilogue: O / l of a finished unit into registers as
+//                  fp16 (O is then free for the next unit), then the output
+//                  rows, while the other warps go on with the next unit.
 //
 // Every wait is bounded (about 2 s); on expiry the kernel records kErrTimeout
 // in the workspace header, stops issuing work, waits (bounded) for its own
@@ -57,7 +57,8 @@ using namespace sm100;
 
 namespace prefill {
 
-constexpr int kThreads = 448;  // 14 warps: 0 loads, 1 MMA, 2-9 softmax, 10-13 epilogue
+constexpr int kThreads = 480;  // 15 warps: 0 loads, 1 S issue, 2-9 softmax, 10-13 epilogue, 14 P V issue
+constexpr int kPvWarp = 14;
 constexpr int kLoadWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kSoftmaxWarp0 = 2;
@@ -66,7 +67,8 @@ constexpr int kEpiWarp0 = kSoftmaxWarp0 + kSoftmaxWarps;
 constexpr int kRows = 128;     // MMA M: query rows of a unit
 constexpr int kKeys = 128;     // keys of a tile: the S tile's N
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kOCol = 256;  // O buffer b at columns 256 + 128 b; S buffer b at 128 b
+constexpr int kSBufs = 3;        // S (then P) buffers in TMEM: tile G uses columns 128 (G % 3) ..
+constexpr uint32_t kOCol = 384;  // the O accumulator: columns 384..511
 constexpr long long kWaitLimit = 4000000000LL;
 
 // Shared memory (offsets from a 1024-byte aligned base).
@@ -84,11 +86,13 @@ struct Shared {
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, pv_done;
-  uint64_t o_full[2], o_empty[2];
+  uint64_t s_full[kSBufs], s_empty[kSBufs];
+  // Per S buffer (tile G uses buffer G % 3): the softmax may run up to three
+  // tiles ahead of P V, so each tile's hand-offs have their own barriers.
+  uint64_t p_full[kSBufs], pv_done[kSBufs];
+  uint64_t o_full, o_empty;
   uint64_t st_full[2], st_empty[2];
-  uint64_t mma_final;
+  uint64_t mma_final, pv_final;
   uint32_t tmem_base;
   int32_t abort_flag;
   int32_t num_units;
@@ -232,43 +236,43 @@ struct PvTile {
 // P V has completed.
 __device__ __forceinline__ bool issue_pv(Shared* sh, const Args& a, uint32_t tmem, uint32_t v_base,
                                          const PvTile& t) {
-  const int ob = t.k & 1, slot = t.G & 1;
-  if (!wt(sh, a.hdr, &sh->p_full, t.G & 1) || !wt(sh, a.hdr, &sh->v_full[slot], (t.G >> 1) & 1) ||
-      (t.j == 0 && !wt(sh, a.hdr, &sh->o_empty[ob], ((t.k >> 1) & 1) ^ 1)))
+  const int slot = t.G & 1, sbuf = t.G % kSBufs;
+  if (!wt(sh, a.hdr, &sh->p_full[sbuf], (t.G / kSBufs) & 1) || !wt(sh, a.hdr, &sh->v_full[slot], (t.G >> 1) & 1) ||
+      (t.j == 0 && !wt(sh, a.hdr, &sh->o_empty, (t.k & 1) ^ 1)))
     return false;
   tc_fence_after();
   const uint32_t idesc = idesc_f16_f32(kRows, 128, false, true);
   const uint64_t vb0 = smem_desc_sw128(v_base + slot * kTile, kHalf, 1024);
-  const uint32_t ocol = tmem + kOCol + 128u * ob, pcol = tmem + 128u * slot;
+  const uint32_t ocol = tmem + kOCol, pcol = tmem + 128u * sbuf;
 #pragma unroll
   for (int kb = 0; kb < kKeys / 16; ++kb)
     mma_f16_ta(ocol, pcol + 8u * kb, vb0 + ((kb * 2048) >> 4), idesc, (t.j > 0 || kb > 0) ? 1u : 0u);
   mma_commit(&sh->v_empty[slot]);
-  mma_commit(&sh->s_empty[slot]);
-  mma_commit(&sh->pv_done);
-  if (t.j == t.nt - 1) mma_commit(&sh->o_full[ob]);
+  mma_commit(&sh->s_empty[sbuf]);
+  mma_commit(&sh->pv_done[sbuf]);
+  if (t.j == t.nt - 1) mma_commit(&sh->o_full);
   return true;
 }
 
+// S = Q K^T of every tile, into S buffer G % 3 once the P V that last read
+// that buffer (tile G - 3) has completed.
 __device__ __noinline__ void mma_role(Shared* sh, const Args& a, uint8_t* smem) {
   const uint32_t tmem = sh->tmem_base;
   const uint32_t q_base = smem_u32(smem + kQOff), k_base = smem_u32(smem + kKOff);
-  const uint32_t v_base = smem_u32(smem + kVOff);
   const uint32_t idesc_s = idesc_f16_f32(kRows, kKeys, false, false);
   Cursor cur;
   cur.init(a.units, sh->num_units);
   Unit u;
-  PvTile prev{0, 0, 0, 0};
-  bool have_prev = false, ok = true;
+  bool ok = true;
   int G = 0;
   for (int k = 0; ok && cur.next(u); ++k) {
     const int qb = k & 1, nt = tiles_of(u, a.tq);
     if (!wt(sh, a.hdr, &sh->q_full[qb], (k >> 1) & 1)) break;
     const uint64_t a0 = smem_desc_sw128(q_base + qb * kTile, 16, 1024);
     for (int j = 0; j < nt; ++j, ++G) {
-      const int slot = G & 1;
+      const int slot = G & 1, sbuf = G % kSBufs;
       if (!wt(sh, a.hdr, &sh->k_full[slot], (G >> 1) & 1) ||
-          !wt(sh, a.hdr, &sh->s_empty[slot], ((G >> 1) & 1) ^ 1)) {
+          !wt(sh, a.hdr, &sh->s_empty[sbuf], ((G / kSBufs) & 1) ^ 1)) {
         ok = false;
         break;
       }
@@ -276,23 +280,38 @@ __device__ __noinline__ void mma_role(Shared* sh, const Args& a, uint8_t* smem) 
       const uint64_t b0 = smem_desc_sw128(k_base + slot * kTile, 16, 1024);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        mma_f16(tmem + 128u * slot, a0 + (((kk >> 2) * kHalf + (kk & 3) * 32) >> 4),
+        mma_f16(tmem + 128u * sbuf, a0 + (((kk >> 2) * kHalf + (kk & 3) * 32) >> 4),
                 b0 + (((kk >> 2) * kHalf + (kk & 3) * 32) >> 4), idesc_s, kk > 0 ? 1u : 0u);
-      mma_commit(&sh->s_full[slot]);
+      mma_commit(&sh->s_full[sbuf]);
       mma_commit(&sh->k_empty[slot]);
       if (j == nt - 1) mma_commit(&sh->q_empty[qb]);
-      if (have_prev && !issue_pv(sh, a, tmem, v_base, prev)) {
-        ok = false;
-        break;
-      }
-      prev = PvTile{G, k, j, nt};
-      have_prev = true;
     }
   }
-  if (ok && have_prev) issue_pv(sh, a, tmem, v_base, prev);
   // Every MMA issued has completed before the CTA frees its tensor memory.
   mma_commit(&sh->mma_final);
   mbar_wait(&sh->mma_final, 0, kWaitLimit);
+}
+
+// O += P V of every tile, by its own thread, so that P V is issued as soon as
+// P is written whatever S the other issuer is waiting to issue.
+__device__ __noinline__ void pv_role(Shared* sh, const Args& a, uint8_t* smem) {
+  const uint32_t tmem = sh->tmem_base;
+  const uint32_t v_base = smem_u32(smem + kVOff);
+  Cursor cur;
+  cur.init(a.units, sh->num_units);
+  Unit u;
+  int G = 0;
+  bool ok = true;
+  for (int k = 0; ok && cur.next(u); ++k) {
+    const int nt = tiles_of(u, a.tq);
+    for (int j = 0; j < nt; ++j, ++G)
+      if (!issue_pv(sh, a, tmem, v_base, PvTile{G, k, j, nt})) {
+        ok = false;
+        break;
+      }
+  }
+  mma_commit(&sh->pv_final);
+  mbar_wait(&sh->pv_final, 0, kWaitLimit);
 }
 
 // ---------------------------------------------------------------- softmax
@@ -346,8 +365,8 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
     for (int x = 0; x < 2; ++x) vis[x] = min(u.qs + row[x] / a.gqa + 1, u.n);
     float m[2] = {neg_inf(), neg_inf()}, l[2] = {0.f, 0.f};
     for (int j = 0; j < nt; ++j, ++G) {
-      const int sb = G & 1;
-      if (!wt_warp(sh, a.hdr, &sh->s_full[sb], (G >> 1) & 1)) {
+      const int sb = G % kSBufs;
+      if (!wt_warp(sh, a.hdr, &sh->s_full[sb], (G / kSBufs) & 1)) {
         ok = false;
         break;
       }
@@ -389,12 +408,12 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
       }
       if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
         // O is complete up to the previous tile once its P V has completed.
-        if (!wt_warp(sh, a.hdr, &sh->pv_done, (G - 1) & 1)) {
+        if (!wt_warp(sh, a.hdr, &sh->pv_done[(G - 1) % kSBufs], ((G - 1) / kSBufs) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        rescale_o(tmem + kOCol + 128u * ob, alpha[0], alpha[1]);
+        rescale_o(tmem + kOCol, alpha[0], alpha[1]);
       }
       uint32_t pk[32];  // register 2R: row a, 2R + 1: row b (16x128b order)
 #pragma unroll
@@ -414,7 +433,7 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
       tmem_st_16x128b_x16(scol, pk);
       tmem_wait_st();
       tc_fence_before();
-      warp_arrive(&sh->p_full);
+      warp_arrive(&sh->p_full[sb]);
     }
     if (!ok) break;
 #pragma unroll
@@ -443,31 +462,30 @@ __device__ __noinline__ void epilogue_role(Shared* sh, const Args& a, uint8_t* s
   Unit u;
   for (int k = 0; cur.next(u); ++k) {
     const int ob = k & 1;
-    if (!wt_warp(sh, a.hdr, &sh->st_full[ob], (k >> 1) & 1) || !wt_warp(sh, a.hdr, &sh->o_full[ob], (k >> 1) & 1))
-      break;
+    if (!wt_warp(sh, a.hdr, &sh->st_full[ob], (k >> 1) & 1) || !wt_warp(sh, a.hdr, &sh->o_full, k & 1)) break;
     tc_fence_after();
     const float inv = 1.f / stats[ob * kRows + row];
-    const int t = u.qs + tok_in_unit;
-    const bool valid = t < u.n;
-    __half* dst = a.o + (long long)(u.ts + t) * a.o_stride + (long long)(u.h * a.gqa + head_in_unit) * kHeadDim;
-#pragma unroll 1
+    uint32_t h[64];
+#pragma unroll
     for (int c = 0; c < 128; c += 32) {
       uint32_t r[32];
-      tmem_ld_32x32b_x16(tmem + kOCol + 128u * ob + c, r);
-      tmem_ld_32x32b_x16(tmem + kOCol + 128u * ob + c + 16, r + 16);
+      tmem_ld_32x32b_x16(tmem + kOCol + c, r);
+      tmem_ld_32x32b_x16(tmem + kOCol + c + 16, r + 16);
       tmem_wait_ld();
-      uint32_t h[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) h[i] = f2_to_h2(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
-      if (valid) {
-        uint4* d4 = reinterpret_cast<uint4*>(dst + c);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) d4[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
-      }
+      for (int i = 0; i < 16; ++i)
+        h[c / 2 + i] = f2_to_h2(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
     }
     tc_fence_before();
-    warp_arrive(&sh->o_empty[ob]);
+    warp_arrive(&sh->o_empty);
     warp_arrive(&sh->st_empty[ob]);
+    const int t = u.qs + tok_in_unit;
+    if (t < u.n) {
+      uint4* d4 = reinterpret_cast<uint4*>(a.o + (long long)(u.ts + t) * a.o_stride +
+                                           (long long)(u.h * a.gqa + head_in_unit) * kHeadDim);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) d4[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+    }
   }
 }
 
@@ -487,15 +505,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sh->k_empty[i], 1);
       mbar_init(&sh->v_full[i], 1);
       mbar_init(&sh->v_empty[i], 1);
-      mbar_init(&sh->s_full[i], 1);
-      mbar_init(&sh->s_empty[i], 1);
-      mbar_init(&sh->o_full[i], 1);
-      mbar_init(&sh->o_empty[i], 4);
+
       mbar_init(&sh->st_full[i], kSoftmaxWarps);
       mbar_init(&sh->st_empty[i], 4);
     }
-    mbar_init(&sh->p_full, kSoftmaxWarps);
-    mbar_init(&sh->pv_done, 1);
+    for (int i = 0; i < kSBufs; ++i) {
+      mbar_init(&sh->s_full[i], 1);
+      mbar_init(&sh->s_empty[i], 1);
+      mbar_init(&sh->p_full[i], kSoftmaxWarps);
+      mbar_init(&sh->pv_done[i], 1);
+    }
+    mbar_init(&sh->o_full, 1);
+    mbar_init(&sh->o_empty, 4);
+    mbar_init(&sh->pv_final, 1);
+
     mbar_init(&sh->mma_final, 1);
     sh->abort_flag = 0;
     fence_mbar_init();
@@ -520,6 +543,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) load_role(sh, args, smem, &tmap_q, &tmap_k, &tmap_v);
   } else if (warp == kMmaWarp) {
     if (lane == 0) mma_role(sh, args, smem);
+  } else if (warp == kPvWarp) {
+    if (lane == 0) pv_role(sh, args, smem);
   } else if (warp >= kSoftmaxWarp0 && warp < kEpiWarp0) {
     softmax_role(sh, args, smem);
   } else {
