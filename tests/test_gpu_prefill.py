@@ -68,6 +68,26 @@ def test_many_short_prompts_and_a_strided_q(cuda):
     torch.testing.assert_close(out.float(), _fp32(q, k, v, cu, scale), atol=ATOL, rtol=RTOL)
 
 
+def test_a_thousand_tiny_prompts_with_a_loose_max_seqlen(cuda):
+    """The plan orders 1,000 prompts of 1-8 tokens (many units per level) and
+    takes a max_seqlen far above the real lengths (empty levels)."""
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    g = torch.Generator().manual_seed(9)
+    lens = torch.randint(1, 9, (1000,), generator=g).tolist()
+    q, k, v, cu = _case(lens, 32, 8, 21, cuda)
+    out = flash_attn_varlen_func(q, k, v, cu, cu, 4096, 4096, softmax_scale=0.1, causal=True)
+    torch.testing.assert_close(out.float(), _fp32(q, k, v, cu, 0.1), atol=ATOL, rtol=RTOL)
+
+
+def test_long_prompt_at_the_draft_ratio(cuda):
+    """Qwen3-0.6B heads (16 q / 8 kv, 64 tokens per unit), one 3,000-token prompt and a short one."""
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    lens = [3000, 70]
+    q, k, v, cu = _case(lens, 16, 8, 33, cuda)
+    out = flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=128 ** -0.5, causal=True)
+    torch.testing.assert_close(out.float(), _fp32(q, k, v, cu, 128 ** -0.5), atol=ATOL, rtol=RTOL)
+
+
 def test_large_scores_move_the_running_max(cuda):
     """Scores whose row max grows along the keys (rescaled O) and spans > 2^8 in exp2."""
     from nebulasd_b200.kernels import flash_attn_varlen_func
