@@ -102,3 +102,16 @@ def norm_rope_case():
     k_w = (1 + 0.02 * torch.randn((d,), generator=g)).half()
     positions = torch.tensor([0, 1, 700, 4095, 30000])
     return dict(q=q, k=k, q_w=q_w, k_w=k_w, eps=1e-6, positions=positions, theta=1e6)
+
+
+def prefill_case():
+    """Inputs for causal prefill attention: six prompts (one empty) of 0-129
+    tokens, 4 q heads over 1 kv head (ratio 4), head dim 128."""
+    g = torch.Generator().manual_seed(707)
+    lens = [1, 17, 40, 129, 0, 33]
+    t, h, hk, d = sum(lens), 4, 1, 128
+    q = torch.randn((t, h, d), generator=g).half()
+    k = torch.randn((t, hk, d), generator=g).half()
+    v = torch.randn((t, hk, d), generator=g).half()
+    cu = torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32)
+    return dict(q=q, k=k, v=v, cu_seqlens=cu, max_seqlen=max(lens), softmax_scale=d ** -0.5)

@@ -11,6 +11,9 @@ The ``swiftllm`` package is mounted as a namespace module (its ``__init__``
 imports the serving stack, which needs ``ray`` and a compiled extension that
 the kernels themselves do not use).
 
+The prefill fixture comes from the layer module's own ``flash_attn_varlen_func``
+(plain PyTorch, run on the CPU); ``--only prefill`` regenerates just that one.
+
 Outputs: ``tests/golden/<case>.npz`` holding the reference outputs, the sha256
 of the inputs (so a test can prove it rebuilt identical inputs) and, for pure
 byte work, only digests.
@@ -65,10 +68,26 @@ def infer_state_for(LlamaInferState, *, seq_ids, decoding_seq_lens, num_prefill_
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path, help="NebulaSD project root")
+    ap.add_argument("--only", choices=("all", "prefill"), default="all",
+                    help="regenerate every fixture, or only prefill.npz")
     args = ap.parse_args()
     paged_attn, kvcache_mgmt, rotary_emb, rmsnorm, LlamaInferState = load_reference(args.reference)
     from tests.golden import cases as C
     from types import SimpleNamespace
+
+    # Prefill: the layer module's own flash_attn_varlen_func (transformer_layer.py:7-32),
+    # a per-prompt scaled_dot_product_attention, run here on the CPU in fp32 on the
+    # fp16-valued inputs.
+    from swiftllm.worker.layers import transformer_layer
+    p = C.prefill_case()
+    o = transformer_layer.flash_attn_varlen_func(p["q"].float(), p["k"].float(), p["v"].float(), p["cu_seqlens"],
+                                                 p["cu_seqlens"], p["max_seqlen"], p["max_seqlen"],
+                                                 softmax_scale=p["softmax_scale"], causal=True)
+    np.savez(HERE / "prefill.npz", o=o.numpy().astype(np.float16),  # fp32 result, stored rounded to fp16
+             input_sha256=C.digest(p["q"], p["k"], p["v"], p["cu_seqlens"]))
+    print("prefill", tuple(o.shape))
+    if args.only == "prefill":
+        return
 
     for name, c in C.attention_cases().items():
         r, h, d = c["q"].shape

@@ -1,11 +1,13 @@
 """GPU: causal prefill attention over packed variable-length sequences (the
 drop-in for ``flash_attn_varlen_func``, ``transformer_layer.py:7-32``) against
-an fp32 per-sequence restatement and against the reference's own function.
+the oracle's fp32 per-prompt restatement (``oracle/prefill.py``), the golden
+fixture made from the reference's own function, and that function itself.
 Tolerance: |ours - fp32| <= 2e-3 + 1e-2 |fp32| (fp16 P and output)."""
 import pytest
 import torch
 
 from baseline import reference as R
+from oracle.prefill import prefill_attention
 
 pytestmark = pytest.mark.gpu
 ATOL, RTOL = 2e-3, 1e-2
@@ -23,20 +25,21 @@ def _case(lens, heads, kv_heads, seed, dev, q_pad=0):
 
 
 def _fp32(q, k, v, cu, scale):
-    out = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
-    c = cu.tolist()
-    rep = q.shape[1] // k.shape[1]
-    for s, e in zip(c[:-1], c[1:]):
-        if e == s:
-            continue
-        qi = q[s:e].float().transpose(0, 1)
-        ki = k[s:e].float().transpose(0, 1).repeat_interleave(rep, 0)
-        vi = v[s:e].float().transpose(0, 1).repeat_interleave(rep, 0)
-        att = (qi @ ki.transpose(1, 2)) * scale
-        n = e - s
-        att = att.masked_fill(torch.triu(torch.ones(n, n, dtype=torch.bool, device=q.device), 1), float("-inf"))
-        out[s:e] = (att.softmax(-1) @ vi).transpose(0, 1)
-    return out
+    return prefill_attention(q, k, v, cu, scale)
+
+
+def test_matches_the_golden_fixture(cuda):
+    """The seeded inputs of the fixture made from the reference's own function."""
+    import numpy as np
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    from tests.golden import cases as C
+    p = C.prefill_case()
+    g = np.load(C.__file__.rsplit("/", 1)[0] + "/prefill.npz")
+    assert str(g["input_sha256"]) == C.digest(p["q"], p["k"], p["v"], p["cu_seqlens"])
+    out = flash_attn_varlen_func(p["q"].to(cuda), p["k"].to(cuda), p["v"].to(cuda), p["cu_seqlens"].to(cuda),
+                                 p["cu_seqlens"].to(cuda), p["max_seqlen"], p["max_seqlen"],
+                                 softmax_scale=p["softmax_scale"], causal=True)
+    torch.testing.assert_close(out.float().cpu(), torch.from_numpy(g["o"]).float(), atol=ATOL, rtol=RTOL)
 
 
 @pytest.mark.parametrize("lens,heads,kv_heads", [

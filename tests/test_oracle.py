@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle import accept, attention, hostkv, kv_store, qk_rope
+from oracle import accept, attention, hostkv, kv_store, prefill, qk_rope
 from tests.golden import cases as C
 
 GOLDEN = C.__file__.rsplit("/", 1)[0]
@@ -84,6 +84,16 @@ def test_qk_norm_rope_oracle_matches_reference_golden():
     # The fp32 restatement is within the fp16 tolerance.
     q32 = qk_rope.rope(torch.from_numpy(g["q_norm"]), cos, sin)
     torch.testing.assert_close(q32.float(), torch.from_numpy(g["q_rope"]).float(), atol=ATOL, rtol=RTOL)
+
+
+def test_prefill_oracle_matches_reference_golden():
+    """Against the layer module's own flash_attn_varlen_func (transformer_layer.py:7-32),
+    run in fp32 on the same inputs; the fixture stores it rounded to fp16."""
+    p = C.prefill_case()
+    g = _load("prefill")
+    assert str(g["input_sha256"]) == C.digest(p["q"], p["k"], p["v"], p["cu_seqlens"])
+    o = prefill.prefill_attention(p["q"], p["k"], p["v"], p["cu_seqlens"], p["softmax_scale"])
+    torch.testing.assert_close(o, torch.from_numpy(g["o"]).float(), atol=1e-3, rtol=2 ** -10)
 
 
 # Known answers of swiftLLM/tests/test_speculative_planning.py:25-178.
