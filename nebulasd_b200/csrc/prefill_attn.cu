@@ -387,7 +387,10 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
               if (8 * R + e >= lim) s[4 * R + 2 * x + e] = __float_as_uint(neg_inf());
         }
       }
+      // Row a's max then its P, then row b's: row b's max (ALU) can issue
+      // while row a's exp2 and packing (XU) are in flight.
       float alpha[2];
+      uint32_t pk[32];  // register 2R: row a, 2R + 1: row b (16x128b order)
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         float t[4] = {neg_inf(), neg_inf(), neg_inf(), neg_inf()};
@@ -405,19 +408,6 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
           alpha[x] = fast_exp2(m[x] - mxs);
           m[x] = mxs;
         }
-      }
-      if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
-        // O is complete up to the previous tile once its P V has completed.
-        if (!wt_warp(sh, a.hdr, &sh->pv_done[(G - 1) % kSBufs], ((G - 1) / kSBufs) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        rescale_o(tmem + kOCol, alpha[0], alpha[1]);
-      }
-      uint32_t pk[32];  // register 2R: row a, 2R + 1: row b (16x128b order)
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
         const float negm = -m[x];
         float acc[2] = {0.f, 0.f};
 #pragma unroll
@@ -429,6 +419,15 @@ __device__ __noinline__ void softmax_role(Shared* sh, const Args& a, uint8_t* sm
           acc[R & 1] += f.x + f.y;
         }
         l[x] = l[x] * alpha[x] + (acc[0] + acc[1]);
+      }
+      if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+        // O is complete up to the previous tile once its P V has completed.
+        if (!wt_warp(sh, a.hdr, &sh->pv_done[(G - 1) % kSBufs], ((G - 1) / kSBufs) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        rescale_o(tmem + kOCol, alpha[0], alpha[1]);
       }
       tmem_st_16x128b_x16(scol, pk);
       tmem_wait_st();
