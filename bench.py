@@ -980,6 +980,25 @@ def run_prefill(args):
         line["reference_gpu"] = {"impl": "the reference's flash_attn_varlen_func (per-prompt SDPA, host sync)",
                                  "ms": round(ref_ms, 4), "speedup": round(ref_ms / ms, 3),
                                  "max_abs_diff": err}
+        # One 8,192-token prompt: the reference's loop is then a single SDPA call.
+        n1 = 8192
+        q1 = torch.randn((n1, heads, dim), generator=gd, device=dev).half()
+        k1 = torch.randn((n1, kv_heads, dim), generator=gd, device=dev).half()
+        v1 = torch.randn((n1, kv_heads, dim), generator=gd, device=dev).half()
+        cu1 = torch.tensor([0, n1], dtype=torch.int32, device=dev)
+        ours_1 = _time_steps(lambda: flash_attn_varlen_func(q1, k1, v1, cu1, cu1, n1, n1, softmax_scale=scale),
+                             steps, warm)
+        for _ in range(warm):
+            ref_fn(q1, k1, v1, cu1, cu1, n1, n1, softmax_scale=scale, causal=True)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            ref_fn(q1, k1, v1, cu1, cu1, n1, n1, softmax_scale=scale, causal=True)
+        torch.cuda.synchronize()
+        ref_1 = (time.perf_counter() - t0) / steps * 1e3
+        fl1 = 4 * heads * dim * n1 * (n1 + 1) / 2
+        line["one_prompt_8k"] = {"ours_ms": round(ours_1, 4), "ours_tflops": round(fl1 / ours_1 / 1e9, 1),
+                                 "reference_ms": round(ref_1, 4), "reference_tflops": round(fl1 / ref_1 / 1e9, 1)}
     print(json.dumps(line), flush=True)
 
 
