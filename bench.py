@@ -263,6 +263,8 @@ def run_ours(args):
         secondary["long_verify_8b_k4"] = _guard(lambda: secondary_attention("long_verify_8b_k4", dev, 3))
         secondary["long_verify_8b_k8"] = _guard(lambda: secondary_attention("long_verify_8b_k8", dev, 3))
         secondary["long_verify_8b_k4_hostkv"] = _guard(lambda: long_hostkv_line("long_verify_8b_k4", dev, 10))
+        secondary["prefill_8b"] = _guard(lambda: prefill_line(dev, 10, 3))
+        secondary["greedy_accept_8b"] = _guard(lambda: accept_line(dev, 50, 3))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -830,17 +832,12 @@ def run_fused(args):
     print(json.dumps(line), flush=True)
 
 
-def run_accept(args):
+def accept_line(dev, steps_arg, warmup_arg, requests=None):
     """Greedy acceptance of a Qwen3-8B verify batch (16 requests x (k+1 = 5)
     rows x 151,936 fp16 logits, 24.3 MB): the device kernel (arg-max and
     acceptance, results left on the GPU) against the reference's tail on the
     same GPU: ``torch.argmax``, ``.tolist()`` and ``compute_greedy_acceptance``
     per request (``post_layer.py:72``, ``model.py:465``, ``speculative.py:122-156``)."""
-    world, rank, local = _dist()
-    if rank != 0:
-        return
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     from nebulasd_b200.accept import greedy_accept
     from baseline import reference as R
     reqs, depth, vocab = 16, 4, 151936
@@ -873,8 +870,8 @@ def run_accept(args):
         greedy_accept(logits, row_start, flat, out=(tokens, count, accepted, amax))
         return result.cpu()
 
-    steps = max(args.steps, 50)
-    us = _time_queued(kernel_only, steps, max(args.warmup, 3)) * 1e3
+    steps = max(steps_arg, 50)
+    us = _time_queued(kernel_only, steps, max(warmup_arg, 3)) * 1e3
     for _ in range(3):
         api()
     t0 = time.perf_counter()
@@ -885,7 +882,7 @@ def run_accept(args):
     peak, peak_kind = _peaks()
     achieved = moved / (us * 1e-6) / 1e9
     line = {"metric": "greedy accept us per verify batch (Qwen3-8B: 16 requests x 5 rows x 151,936 logits)",
-            "value": round(us, 2), "unit": "us", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 3),
+            "value": round(us, 2), "unit": "us", "n_gpus": 1, "steps": steps, "warmup": max(warmup_arg, 3),
             "higher_is_better": False, "scaling": "none", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "greedy_accept_8b", "requests": reqs, "depth": depth, "vocab": vocab,
                        "l2": "the 24.3 MB of logits fit L2, as they do after the lm_head GEMM that writes them"},
@@ -912,10 +909,19 @@ def run_accept(args):
         ref_us = (time.perf_counter() - t0) / 20 * 1e6
         line["reference_gpu"] = {"impl": "torch.argmax + .tolist() + compute_greedy_acceptance (host), same logits",
                                  "us": round(ref_us, 2), "host_sync": True}
+    return line
+
+
+def run_accept(args):
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    line = accept_line(torch.device("cuda", local), args.steps, args.warmup, args.requests)
     print(json.dumps(line), flush=True)
 
 
-def run_prefill(args):
+def prefill_line(dev, steps_arg, warmup_arg, requests=None):
     """Causal prefill attention of one Qwen3-8B layer (32 q / 8 kv heads, head
     dim 128) over a packed batch of ragged prompts (seeded lengths U[64, 2048],
     --requests prompts, default 16): the drop-in ``flash_attn_varlen_func``
@@ -923,14 +929,9 @@ def run_prefill(args):
     reference's own function on the same GPU (``transformer_layer.py:7-32``:
     ``cu_seqlens`` to the host, one ``scaled_dot_product_attention`` per
     prompt).  q, k and v (about 170 MB) are larger than L2."""
-    world, rank, local = _dist()
-    if rank != 0:
-        return
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     from nebulasd_b200.kernels import flash_attn_varlen_func
     from baseline import reference as R
-    nseq = args.requests or 16
+    nseq = requests or 16
     g = torch.Generator().manual_seed(4242)
     lens = torch.randint(64, 2049, (nseq,), generator=g).tolist()
     heads, kv_heads, dim = 32, 8, 128
@@ -945,7 +946,7 @@ def run_prefill(args):
     def ours():
         return flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), softmax_scale=scale, causal=True)
 
-    steps, warm = max(args.steps, 20), max(args.warmup, 3)
+    steps, warm = max(steps_arg, 20), max(warmup_arg, 3)
     ms = _time_steps(ours, steps, warm)
     # QK^T and PV over the causal triangle: 4 * heads * dim FLOPs per (query, key) pair
     flops = sum(4 * heads * dim * n * (n + 1) / 2 for n in lens)
@@ -999,6 +1000,15 @@ def run_prefill(args):
         fl1 = 4 * heads * dim * n1 * (n1 + 1) / 2
         line["one_prompt_8k"] = {"ours_ms": round(ours_1, 4), "ours_tflops": round(fl1 / ours_1 / 1e9, 1),
                                  "reference_ms": round(ref_1, 4), "reference_tflops": round(fl1 / ref_1 / 1e9, 1)}
+    return line
+
+
+def run_prefill(args):
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    line = prefill_line(torch.device("cuda", local), args.steps, args.warmup, args.requests)
     print(json.dumps(line), flush=True)
 
 
