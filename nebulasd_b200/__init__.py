@@ -30,12 +30,13 @@ _ALIASES = {
 def install() -> None:
     """Route the reference's attention ops to this package.
 
-    Patches the reference modules' attributes if they are already imported (and
-    ``swiftllm.worker.layers.transformer_layer``'s module-level names, which it
-    binds at import), and otherwise installs the replacements so later imports
-    resolve to them.  Only the names listed in ``_ALIASES`` change; everything
-    else in those modules (e.g. ``fused_add_rmsnorm_inplace``) stays the
-    reference's.
+    Patches the attributes of the reference modules that are already imported:
+    the kernel modules' functions, ``swiftllm.worker.layers.transformer_layer``'s
+    module-level names (which it binds at import) including its own
+    ``flash_attn_varlen_func``, and ``nebulasd.kv.cuda_transfer.CudaCopyBackend``.
+    Modules not yet imported are left alone, so call it after importing the
+    reference.  Only these names change; everything else in those modules (e.g.
+    ``fused_add_rmsnorm_inplace``) stays the reference's.
     """
     from . import kernels
     for mod_name, names in _ALIASES.items():
