@@ -190,3 +190,22 @@ def test_accept_batch_validates_like_the_reference():
         compute_greedy_acceptance_batch([[1, 2, 3, 4, 5]], logits)
     with _pytest.raises(ValueError, match="non-negative"):
         compute_greedy_acceptance_batch([[1, 2, 3, 4]], logits, remaining_output_len=[-1])
+
+
+def test_prefill_drop_in_rejects_bad_arguments_on_the_host():
+    """flash_attn_varlen_func's checks, as the reference's callers would meet them (no GPU needed)."""
+    import torch
+    from nebulasd_b200.kernels import flash_attn_varlen_func
+    q = torch.zeros((10, 8, 128), dtype=torch.float16)
+    k = torch.zeros((10, 2, 128), dtype=torch.float16)
+    cu = torch.tensor([0, 4, 10], dtype=torch.int32)
+    with pytest.raises(NotImplementedError):
+        flash_attn_varlen_func(q, k, k, cu, cu, 6, 6, causal=False)
+    with pytest.raises(NotImplementedError):
+        flash_attn_varlen_func(q, k, k, cu, torch.tensor([0, 5, 10], dtype=torch.int32), 6, 6)
+    with pytest.raises(TypeError):
+        flash_attn_varlen_func(q.float(), k, k, cu, cu, 6, 6)
+    with pytest.raises(ValueError):
+        flash_attn_varlen_func(q[..., :64], k[..., :64], k[..., :64], cu, cu, 6, 6)
+    with pytest.raises(ValueError):
+        flash_attn_varlen_func(q, k, k, cu.long(), cu.long(), 6, 6)
